@@ -1,0 +1,278 @@
+"""Benchmark of the B200 env step (BASELINE.json metric: agent env-steps/s, skip 4, 84x84x4 obs).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--envs E] [--impl ours|reference]
+    torchrun --nproc-per-node N bench.py --gpus N ...        (one process per GPU, env_offset = rank * E)
+
+Workload = BASELINE config 1: E = 32768 envs per GPU on the synthetic NROM (seed 0), the 32 level names cycled,
+skip 4, sticky 0.25, noop_max 30, maxpool, max_steps 2000, frame_stack 4, uniform random actions over 7.
+`value` is device-timed (CUDA events on the stepping stream, barrier + synchronize on both sides, max over ranks)
+with the actions already in HBM; `e2e` is the same steps through the FastVecEnv host API (pinned host actions
+in, full stacked obs / rewards / dones / infos out, every step). The per-step working set (console slabs, VRAM,
+PPU logs, frame stacks) is several GB, far above the 126 MB L2, so no L2 flush is inserted between steps.
+
+--impl reference times the reference's own CPU engine (oracle/_ref/libfastmario.so, built from the reference's
+csrc by oracle/Makefile) with all host threads on the same config; rank 0 only.
+"""
+from __future__ import annotations
+
+import argparse
+import importlib.util
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+PKG_DIR = os.path.join(ROOT, "fast-mario-env_b200")
+METRIC = "agent env-steps/sec (skip 4, 84x84x4 obs)"
+UNIT = "env-steps/s"
+ALGO_BYTES_PER_STEP = 58582  # algorithmic HBM bytes per env-step (state r/w, stack r/w, scalars, outputs)
+
+
+def load_package():
+    name = "fast_mario_env_b200"
+    if name in sys.modules:
+        return sys.modules[name]
+    spec = importlib.util.spec_from_file_location(name, os.path.join(PKG_DIR, "__init__.py"),
+                                                  submodule_search_locations=[PKG_DIR])
+    mod = importlib.util.module_from_spec(spec)
+    sys.modules[name] = mod
+    spec.loader.exec_module(mod)
+    return mod
+
+
+def workload(args):
+    return dict(workload="config1: synthetic NROM seed 0, 32 levels cycled, skip 4, sticky 0.25, noop_max 30, "
+                         "maxpool, max_steps 2000, frame_stack 4, uniform random actions",
+                n_envs_per_gpu=args.envs, skip=4, frame_stack=4, maxpool=True, sticky=0.25, noop_max=30,
+                max_steps=2000, l2="working set per step >> 126 MB L2 (no flush needed)")
+
+
+def level_names(n):
+    levels = [f"{w}-{s}" for w in range(1, 9) for s in range(1, 5)]
+    return [levels[i % len(levels)] for i in range(n)]
+
+
+def read_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return float(d.get("hbm_gbs", 6650.0)), "measured"
+    return 6650.0, "fallback"
+
+
+def committed_traffic():
+    p = os.path.join(ROOT, "profiles", "k_step_traffic.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return d.get("dram_bytes_per_env_step")
+    return None
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled during the timed region."""
+
+    def __init__(self, gpu_index: int):
+        self.f = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+        q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+             "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+             "clocks_event_reasons.sw_power_cap")
+        try:
+            self.p = subprocess.Popen(["nvidia-smi", f"--id={gpu_index}", f"--query-gpu={q}", "--format=csv,noheader,nounits",
+                                       "-lms", "200"], stdout=self.f, stderr=subprocess.DEVNULL)
+        except Exception:
+            self.p = None
+
+    def stop(self):
+        if self.p is None:
+            return None
+        self.p.terminate()
+        try:
+            self.p.wait(timeout=5)
+        except Exception:
+            self.p.kill()
+        self.f.flush()
+        rows = []
+        for line in open(self.f.name):
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) >= 9:
+                rows.append(parts)
+        os.unlink(self.f.name)
+        if not rows:
+            return None
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[k] for r in rows for k in range(4) if r[5 + k].lower() == "active"})
+        loaded = [s for s in sm] or [0.0]
+        return {"sm_mhz": statistics.median(loaded), "sm_max_mhz": float(rows[0][2]) if rows[0][2].replace(".", "").isdigit() else None,
+                "reasons": reasons, "samples": len(rows)}
+
+
+def cpu_baseline(rom, args, seconds=12.0):
+    """The reference FastVecEnv engine (oracle/_ref) with all host threads, bounded sample."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import ref
+    if not ref.available():
+        return None
+    cores = os.cpu_count() or 1
+    n = 64 * cores
+    levels = [(lambda w, s: (w, s, s + 1 if (w in (1, 2, 4, 7) and s >= 2) else s))(w, s)
+              for w in range(1, 9) for s in range(1, 5)]
+    lv = [levels[i % 32] for i in range(n)]
+    e = ref.RefVecEnv(rom, lv, n, seed=0, sticky=0.25, noop_max=30, maxpool=True, max_steps=2000, n_threads=cores)
+    e.reset()
+    rng = np.random.default_rng(1)
+    for _ in range(5):
+        e.step(rng.integers(0, 7, n))
+    steps, t0 = 0, time.perf_counter()
+    while time.perf_counter() - t0 < seconds:
+        e.step(rng.integers(0, 7, n))
+        steps += 1
+    dt = time.perf_counter() - t0
+    e.close()
+    return {"value": n * steps / dt, "unit": UNIT, "cores": cores, "kind": "reference",
+            "sample": f"{steps} steps x {n} envs ({dt:.1f} s) of the reference FastVecEnv C++ thread pool "
+                      f"(oracle/_ref/libfastmario.so, {cores} threads), same config"}
+
+
+def run_reference(args, rank):
+    if rank != 0:
+        return
+    load_package()
+    from fast_mario_env_b200.synth_rom import build_rom
+    rom = build_rom(0)
+    cb = cpu_baseline(rom, args, seconds=max(5.0, 2.0 * args.steps))
+    if cb is None:
+        print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref/libfastmario.so not built"}))
+        return
+    line = {"impl": "reference", "metric": METRIC, "value": cb["value"], "unit": UNIT, "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": None, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "u8", "data": "synthetic", "config": workload(args),
+            "cpu_baseline": cb, "e2e": {"value": cb["value"], "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line))
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--envs", type=int, default=32768)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        run_reference(args, rank)
+        return
+
+    import torch
+    fme = load_package()
+    from fast_mario_env_b200.synth_rom import build_rom
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    dist = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+
+    rom = build_rom(0)
+    E = args.envs
+    off = rank * E
+    env = fme.CudaVecEnv(level_names(E), E, seed=0, sticky=0.25, noop_max=30, max_steps=2000, skip=4, frame_stack=4,
+                         maxpool=True, device=dev, rom=rom, env_offset=off)
+    total = args.warmup + args.steps
+    g = torch.Generator(device=dev)
+    g.manual_seed(1234 + rank)
+    acts = torch.randint(0, 7, (total, E), dtype=torch.int64, device=dev, generator=g)
+    stream = torch.cuda.current_stream(dev)
+    env.reset()
+    for t in range(args.warmup):
+        env.step(acts[t])
+    torch.cuda.synchronize(dev)
+    env.check()
+    if dist:
+        dist.barrier()
+    clocks = ClockSampler(local)
+    torch.cuda.synchronize(dev)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record(stream)
+    for t in range(args.warmup, total):
+        env.step(acts[t])
+    ev1.record(stream)
+    torch.cuda.synchronize(dev)
+    clk = clocks.stop()
+    ms = ev0.elapsed_time(ev1)
+    env.check()
+    ms_t = torch.tensor([ms], device=dev, dtype=torch.float64)
+    if dist:
+        dist.barrier()
+        dist.all_reduce(ms_t, op=dist.ReduceOp.MAX)
+    ms_max = float(ms_t.item())
+    value = world * E * args.steps / (ms_max / 1000.0)
+    ms_step = ms_max / args.steps
+    kernel_ms = ms / args.steps  # one k_step launch per step on this rank
+
+    # ---- end to end through the FastVecEnv host API (host actions in, host outputs out, every step)
+    e2e = None
+    if not args.no_e2e:
+        fenv = fme.FastVecEnv(level_names(E), E, seed=0, sticky=0.25, noop_max=30, max_steps=2000, maxpool=True,
+                              rom=rom, env_offset=off, device=dev)
+        fenv.reset()
+        hacts = np.random.default_rng(99 + rank).integers(0, 7, (total, E))
+        for t in range(args.warmup):
+            fenv.step(hacts[t])
+        if dist:
+            dist.barrier()
+        t0 = time.perf_counter()
+        for t in range(args.warmup, total):
+            fenv.step(hacts[t])
+        dt = time.perf_counter() - t0
+        fenv.check()
+        dt_t = torch.tensor([dt], device=dev, dtype=torch.float64)
+        if dist:
+            dist.all_reduce(dt_t, op=dist.ReduceOp.MAX)
+        h2d = E * 8
+        d2h = E * (4 * 84 * 84 * 2 + 4 + 1 + 1 + 40 + 8 + 4)
+        e2e = {"value": world * E * args.steps / float(dt_t.item()), "unit": UNIT, "h2d_bytes_per_step": h2d * world,
+               "d2h_bytes_per_step": d2h * world, "api": "FastVecEnv.step (numpy in/out, full stacks, infos)"}
+        fenv.close()
+
+    peak, peak_kind = read_peaks()
+    achieved = ALGO_BYTES_PER_STEP * E / (kernel_ms / 1000.0) / 1e9
+    traffic_per_step = committed_traffic()
+    roofline = {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                "traffic": traffic_per_step * E if traffic_per_step else None,
+                "kernel": "k_step", "algorithmic_bytes_per_env_step": ALGO_BYTES_PER_STEP,
+                "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured" else "fallback 6.65 TB/s",
+                "note": "the env step is an issue-bound integer interpreter; HBM fraction is reported as required, "
+                        "issue-slot figures are in profiles/"}
+    cb = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cb = cpu_baseline(rom, args)
+    if rank == 0:
+        line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+                "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak",
+                "vs_baseline": None, "dtype": "u8", "data": "synthetic", "config": workload(args),
+                "parallelism": f"env shards by env_offset x{world}, no collective", "gpu_launches": args.steps,
+                "roofline": roofline, "cpu_baseline": cb, "e2e": e2e, "clocks": clk}
+        print(json.dumps(line))
+    env.close()
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,138 @@
+// fme_defs.h - constants, data layouts and the opcode decode format shared by host and device code.
+//
+// Layouts (all chosen for the B200 kernels, not taken from the reference):
+//  * Console memory that the 6502 touches every instruction (RAM, OAM, palette) is kept per warp-group
+//    of 32 envs in a "lane-interleaved" slab: 32-bit word w of lane l lives at word (w * 32 + l). In
+//    shared memory every lane therefore owns bank l, so any mix of addresses across the warp is
+//    conflict-free; in HBM the slab is one contiguous 73 KB block that is streamed in and out whole.
+//  * VRAM (2 KB) stays in HBM, contiguous per env: it is touched only by $2007 and the frame snapshot.
+//  * Scalar state (CPU/PPU registers, timing, env bookkeeping) is SoA: word w of env e at w*n_pad + e.
+#pragma once
+#include <stdint.h>
+
+#ifdef __CUDACC__
+#define FME_HD __host__ __device__ __forceinline__
+#define FME_NI __host__ __device__ __noinline__
+#else
+#define FME_HD inline
+#define FME_NI inline
+#include <vector_types.h>
+#endif
+
+namespace fme {
+
+constexpr int RAM_BYTES = 0x800;
+constexpr int VRAM_BYTES = 0x800;
+constexpr int OAM_BYTES = 0x100;
+constexpr int PAL_BYTES = 0x20;
+constexpr int LANES = 32;
+constexpr int SLAB_RAM_OFF = 0;                                  // bytes inside one group's slab
+constexpr int SLAB_OAM_OFF = RAM_BYTES * LANES;                  // 65536
+constexpr int SLAB_PAL_OFF = SLAB_OAM_OFF + OAM_BYTES * LANES;   // 73728
+constexpr int SLAB_BYTES = SLAB_PAL_OFF + PAL_BYTES * LANES;     // 74752
+
+constexpr int FRAME_ITERS = 29781;           // CPU iterations per emulated frame (nes_core.hpp:53)
+constexpr int FRAME_CALLS = 3 * FRAME_ITERS;  // PPU calls per emulated frame
+constexpr int OBS = 84;
+constexpr int OBS_BYTES = OBS * OBS;
+constexpr int SCREEN_W = 256, SCREEN_H = 240;
+
+// status flags (reversed bit order of nes-py's bitfield, N is bit 0; nes_core.hpp:36-38)
+enum : uint32_t { F_N = 0x01, F_V = 0x02, F_ONE = 0x04, F_B = 0x08, F_D = 0x10, F_I = 0x20, F_Z = 0x40, F_C = 0x80 };
+enum : uint32_t { PS_PRE = 0, PS_RENDER = 1, PS_POST = 2, PS_VBLANK = 3 };
+
+// ---------------------------------------------------------------- opcode decode word
+// bits 0-3 kind, 4-7 addressing mode, 8-12 operation, 13 page-cross penalty, 16-23 base cycles.
+enum Kind : uint32_t {
+    K_BAD = 0,      // unimplemented: bad_ops++, nothing else
+    K_BAD_ZP = 1,   // decoded addressing (1 operand byte read) but no operation: bad_ops++
+    K_BAD_ABS = 2,  // 2 operand bytes read, no operation
+    K_BAD_ABSX = 3, // 2 operand bytes read, page-cross penalty with X, no operation
+    K_IMPL = 4,
+    K_BRANCH = 5,
+    K_READ = 6,
+    K_STORE = 7,
+    K_RMW = 8,
+    K_ACC = 9,
+};
+enum Mode : uint32_t { M_NONE = 0, M_IMM, M_ZP, M_ZPX, M_ZPY, M_ABS, M_ABSX, M_ABSY, M_INDX, M_INDY };
+enum ReadOp : uint32_t { R_ORA = 0, R_AND, R_EOR, R_ADC, R_LDA, R_CMP, R_SBC, R_BIT, R_LDX, R_LDY, R_CPX, R_CPY };
+enum StoreOp : uint32_t { W_STA = 0, W_STX, W_STY };
+enum RmwOp : uint32_t { X_ASL = 0, X_ROL, X_LSR, X_ROR, X_DEC, X_INC };
+enum ImplOp : uint32_t {
+    I_BRK = 0, I_PHP, I_CLC, I_JSR, I_PLP, I_SEC, I_RTI, I_PHA, I_JMP, I_CLI, I_RTS, I_PLA, I_JMPI, I_SEI,
+    I_DEY, I_TXA, I_TYA, I_TXS, I_TAY, I_TAX, I_CLV, I_TSX, I_INY, I_DEX, I_CLD, I_INX, I_NOP, I_SED
+};
+FME_HD uint32_t d_kind(uint32_t d) { return d & 15u; }
+FME_HD uint32_t d_mode(uint32_t d) { return (d >> 4) & 15u; }
+FME_HD uint32_t d_op(uint32_t d) { return (d >> 8) & 31u; }
+FME_HD uint32_t d_pen(uint32_t d) { return (d >> 13) & 1u; }
+FME_HD uint32_t d_cycles(uint32_t d) { return (d >> 16) & 255u; }
+
+// ---------------------------------------------------------------- log records (16 B each)
+enum RecType : uint32_t { REC_SEG = 0, REC_VRAM = 1, REC_PAL = 2, REC_OAM = 3, REC_DMA = 4, REC_LIST = 5, REC_VSNAP = 6 };
+// VRAM writes logged one by one between two segments; past this many the next segment is preceded by a
+// whole-VRAM snapshot instead (bulk nametable uploads), which bounds a burst at twice the snapshot size.
+constexpr int VRAM_BURST_MAX = 128;
+// SEG  w0: type | y<<4 | x0<<12 | x1<<21      (visible dots [x0, x1) of line y)
+//      w1: v (16 bits) | fine_x<<16 | render flags<<19
+//      w2: pending-eval bit | eval_y<<1 | oam_addr<<9
+// VRAM w0: type | index<<4 (11 bits) | value<<16       PAL/OAM the same with 5/8-bit index
+// DMA  w0: type, followed by 16 records holding the whole OAM after the copy
+// LIST w0: type | nsl<<4; w1: sl[0..3]; w2: sl[4..7]
+// VSNAP w0: type, followed by 128 records holding the whole 2 KB VRAM
+enum : uint32_t { TOUCH_ALL = 1, TOUCH_BG = 2, TOUCH_SPR = 4, TOUCH_VRAM = 8 };
+enum : uint32_t { RF_SHOW_BG = 1, RF_SHOW_SPR = 2, RF_HIDE_BG = 4, RF_HIDE_SPR = 8, RF_LONG = 16,
+                  RF_BG_PAGE = 32, RF_SPR_PAGE = 64 };
+
+// A log slot: frame-start snapshot (VRAM, palette, OAM, sprite-list state) + record stream.
+constexpr int SLOT_HDR_VRAM = 0;
+constexpr int SLOT_HDR_PAL = 2048;
+constexpr int SLOT_HDR_OAM = 2080;
+constexpr int SLOT_HDR_LIST = 2336;   // 4 words: nsl | pend<<8 | eval_y<<16, sl[0..3], sl[4..7], nrec
+constexpr int SLOT_HDR_BYTES = 2352;  // multiple of 16
+FME_HD size_t slot_bytes(int cap) { return (size_t)SLOT_HDR_BYTES + (size_t)cap * 16u; }
+
+// ---------------------------------------------------------------- scalar state words (SoA)
+enum Scal : int {
+    // console (part of the snapshot / reset image)
+    S_CPU0 = 0,   // pc | a<<16 | x<<24
+    S_CPU1,       // y | sp<<8 | p<<16 | zero_skip<<24
+    S_ITER_LO, S_ITER_HI,  // CPU iteration at the frame boundary (nes-py cycle count)
+    S_EXEC,       // exec_at - iter
+    S_PPUC,       // ppu_calls - 3*iter
+    S_THRESH,     // nmi_thresh - 3*iter
+    S_JOY,        // strobe0 | strobe1<<1 | buttons0<<8 | buttons1<<16
+    S_JOYB,       // bits0 | bits1<<8
+    S_PPU0,       // pstate | scanline<<2 | pcyc<<12 | fine_x<<22 | first_write<<25 | vblank<<26 | s0hit<<27 | even<<28 | inc32<<29
+    S_PPU1,       // v | t<<16
+    S_PPU2,       // data_buffer | oam_addr<<8 | regflags<<16 | nsl<<24
+    S_SL0, S_SL1, // sprite list sl[0..3], sl[4..7]
+    S_CONSOLE_WORDS,
+    // env bookkeeping
+    S_XLAST = S_CONSOLE_WORDS, S_TLAST, S_PREV, S_LIVES, S_T, S_EPLEN, S_EPRET_LO, S_EPRET_HI,
+    S_RNG_S0, S_RNG_S1, S_RNG_S2, S_RNG_S3,  // PCG64 state, least significant word first
+    S_RNG_I0, S_RNG_I1, S_RNG_I2, S_RNG_I3,  // PCG64 increment
+    S_RNG_HAS, S_RNG_U32,                    // numpy has_uint32 / uinteger
+    S_LEVEL, S_FRAMES_LO, S_FRAMES_HI, S_BADOPS, S_STATUS,
+    S_WORDS
+};
+// register flag byte inside S_PPU2 (bits 16-23)
+enum : uint32_t { PF_SHOW_BG = 1, PF_SHOW_SPR = 2, PF_HIDE_BG = 4, PF_HIDE_SPR = 8, PF_LONG = 16, PF_NMI = 32,
+                  PF_BG_PAGE = 64, PF_SPR_PAGE = 128 };
+
+// error / status bits (per env word S_STATUS and the global error word)
+enum : uint32_t {
+    ST_LOG_OVERFLOW = 1u,     // a frame produced more log records than the slot holds
+    ST_HACK_CAP = 2u,         // the busy-state skip loop exceeded its frame cap
+    ST_BOOT_CAP = 4u,         // level boot exceeded its frame cap
+    ST_BAD_ACTION = 8u,       // action outside 0..6 (treated as 0)
+    ST_FRAME_CAP = 16u,       // a frame exceeded its instruction cap
+};
+
+// Console image (contiguous, used for level boot snapshots, the reset cache and raw backups).
+constexpr int IMG_RAM = 0, IMG_VRAM = 2048, IMG_OAM = 4096, IMG_PAL = 4352, IMG_SCAL = 4384;
+constexpr int IMG_BYTES = IMG_SCAL + 4 * S_CONSOLE_WORDS + 8;  // + pad to 16
+constexpr int IMG_STRIDE = (IMG_BYTES + 15) / 16 * 16;
+
+}  // namespace fme

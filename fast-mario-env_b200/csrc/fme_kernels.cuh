@@ -1,0 +1,266 @@
+// fme_kernels.cuh - device side: PCG64, the agent-step state machine, the warp renderer driver and kernels.
+#pragma once
+#include <cuda_runtime.h>
+#include "fme_defs.h"
+
+namespace fme {
+__constant__ uint32_t c_dtab[256];
+extern uint32_t g_host_dtab[256];
+}
+#if defined(__CUDA_ARCH__)
+#define FME_DTAB(op) (::fme::c_dtab[(op)])
+#else
+#define FME_DTAB(op) (::fme::g_host_dtab[(op)])
+#endif
+#include "fme_core.h"
+#include "fme_agent.h"
+#include "fme_render.h"
+
+namespace fme {
+
+__constant__ AreaTabs c_area;
+
+constexpr unsigned FULL = 0xffffffffu;
+
+// ---------------------------------------------------------------- kernel parameters
+struct Dev {
+    int n, n_pad;
+    uint8_t* slab;      // n_pad/32 groups x SLAB_BYTES
+    uint8_t* vram;      // n_pad x 2048
+    uint32_t* scal;     // S_WORDS x n_pad
+    uint8_t* logs;      // n_pad x 2 slots
+    int log_cap;
+    const uint8_t* prg;
+    const uint8_t* chr;
+    uint32_t nt[4];
+    const uint8_t* lut; // 256 gray LUT (global)
+    uint32_t* err;      // global status word
+};
+
+struct StepParams {
+    Dev d;
+    int mode;
+    int skip, max_steps, noop_max, maxpool, frame_stack;
+    int sticky_on;
+    uint64_t sticky_thr;  // draw counts as "repeat" when (next64 >> 11) < sticky_thr
+    int hack_cap;
+    uint64_t simple;      // SIMPLE_MOVEMENT controller bytes, byte k = action k
+    const int64_t* actions;
+    // outputs (MODE_STEP)
+    uint8_t* obs; uint8_t* fin; float* rew; uint8_t* term; uint8_t* trunc; int32_t* info; double* ep_ret;
+    int32_t* ep_len;
+    Cache cache;
+    int n_levels;
+    // MODE_NOOP: where to write the cache entry for this noop step
+    uint8_t* out_img; uint8_t* out_obs; int32_t* out_meta; int noop_j;
+    const uint8_t* level_img; const uint8_t* level_obs0; const int32_t* level_meta;  // backups (x0, t0)
+};
+
+__device__ __forceinline__ size_t slot_off(int e, int s, int cap) {
+    return ((size_t)e * 2 + (size_t)s) * slot_bytes(cap);
+}
+
+// ---------------------------------------------------------------- per-lane console binding
+__device__ __forceinline__ void bind_core(Core& c, const Dev& d, uint8_t* sm, int lane, int e) {
+    c.ram = sm + SLAB_RAM_OFF + lane * 4;
+    c.oam = sm + SLAB_OAM_OFF + lane * 4;
+    c.pal = sm + SLAB_PAL_OFF + lane * 4;
+    c.vram = d.vram + (size_t)e * VRAM_BYTES;
+    c.cart.prg = d.prg; c.cart.chr = d.chr;
+    for (int i = 0; i < 4; i++) c.cart.nt[i] = d.nt[i];
+    c.rec = nullptr; c.nrec = 0; c.cap = 0; c.seg_open = false; c.seg_w0 = 0; c.status = 0; c.seg_idx = 0; c.seg_reads = 0;
+    c.vram_burst = 0; c.vram_dirty = false;
+}
+
+// coalesced copy of a whole slab between HBM and shared memory (warp-wide)
+__device__ __forceinline__ void copy_slab(uint8_t* dst, const uint8_t* src, int lane) {
+    const uint4* s = reinterpret_cast<const uint4*>(src);
+    uint4* d = reinterpret_cast<uint4*>(dst);
+#pragma unroll 4
+    for (int i = lane; i < SLAB_BYTES / 16; i += 32) d[i] = s[i];
+}
+
+// ---------------------------------------------------------------- warp renderer
+// Shared-memory layout of the render phase (reuses the emulation slab region).
+constexpr int RS_FB = 0;                         // 240 x 256
+constexpr int RS_VRAM = RS_FB + SCREEN_W * SCREEN_H;
+constexpr int RS_PAL = RS_VRAM + VRAM_BYTES;
+constexpr int RS_OAM = RS_PAL + PAL_BYTES;
+constexpr int RS_STAGE = RS_OAM + OAM_BYTES;     // one staged row (256)
+constexpr int RS_OBS = RS_STAGE + SCREEN_W;      // 84 x 84 result
+constexpr int RS_END = RS_OBS + OBS_BYTES;
+static_assert(RS_END <= SLAB_BYTES, "render scratch must fit the slab region");
+
+// Replay one logged frame into the framebuffer. raw: palette values (screen) instead of gray.
+// max_mode: combine with the frame already in the framebuffer by max (ALE-style max-pool).
+__device__ void render_slot(const uint8_t* slot, uint8_t* sm, const Dev& d, bool raw, bool max_mode, int lane) {
+    uint8_t* fb = sm + RS_FB;
+    RState rs;
+    rs.vram = sm + RS_VRAM; rs.pal = sm + RS_PAL; rs.oam = sm + RS_OAM; rs.chr = d.chr;
+    for (int i = 0; i < 4; i++) rs.nt[i] = d.nt[i];
+    uint8_t* stage = sm + RS_STAGE;
+    {
+        const uint4* hv = reinterpret_cast<const uint4*>(slot + SLOT_HDR_VRAM);
+        uint4* sv = reinterpret_cast<uint4*>(rs.vram);
+        for (int i = lane; i < VRAM_BYTES / 16; i += 32) sv[i] = hv[i];
+        if (lane < PAL_BYTES / 4)
+            reinterpret_cast<uint32_t*>(rs.pal)[lane] = reinterpret_cast<const uint32_t*>(slot + SLOT_HDR_PAL)[lane];
+        for (int i = lane; i < OAM_BYTES / 4; i += 32)
+            reinterpret_cast<uint32_t*>(rs.oam)[i] = reinterpret_cast<const uint32_t*>(slot + SLOT_HDR_OAM)[i];
+    }
+    const uint32_t* lw = reinterpret_cast<const uint32_t*>(slot + SLOT_HDR_LIST);
+    rs.nsl = lw[0] & 0xffu; rs.sl_lo = lw[1]; rs.sl_hi = lw[2];
+    const int nrec = (int)lw[3] < d.log_cap ? (int)lw[3] : d.log_cap;
+    const uint4* recs = reinterpret_cast<const uint4*>(slot + SLOT_HDR_BYTES);
+    __syncwarp();
+    int first_row = -1;
+    uint32_t lkey = 0xffffffffu, lnsl = 0, llo = 0, lhi = 0;
+    uint32_t oam_ver = 0;
+    for (int r = 0; r < nrec; r++) {
+        uint4 rec = recs[r];
+        uint32_t type = rec.x & 15u;
+        if (type == REC_SEG) {
+            Seg g = decode_seg(rec);
+            uint32_t nsl, lo, hi;
+            if (g.pend) {
+                uint32_t key = g.ev_y | (g.oam_addr << 8) | ((g.flags & RF_LONG) ? 0x10000u : 0u) | (oam_ver << 17);
+                if (key != lkey) {
+                    int start = (int)(g.oam_addr >> 2);
+                    int range = (g.flags & RF_LONG) ? 16 : 8;
+                    int d0 = (int)g.ev_y - (int)rs.oam[lane * 4];
+                    int d1 = (int)g.ev_y - (int)rs.oam[(lane + 32) * 4];
+                    bool in0 = lane >= start && d0 >= 0 && d0 < range;
+                    bool in1 = lane + 32 >= start && d1 >= 0 && d1 < range;
+                    uint64_t m = (uint64_t)__ballot_sync(FULL, in0) | ((uint64_t)__ballot_sync(FULL, in1) << 32);
+                    uint32_t n = 0, lo_ = 0, hi_ = 0;
+                    while (m && n < 8) {
+                        uint32_t i = (uint32_t)(__ffsll((long long)m) - 1);
+                        m &= m - 1;
+                        if (n < 4) lo_ |= i << (8 * n); else hi_ |= i << (8 * (n - 4));
+                        n++;
+                    }
+                    lkey = key; lnsl = n; llo = lo_; lhi = hi_;
+                }
+                nsl = lnsl; lo = llo; hi = lhi;
+            } else {
+                nsl = rs.nsl; lo = rs.sl_lo; hi = rs.sl_hi;
+            }
+            if (max_mode && first_row < 0) first_row = g.y;
+            const bool to_stage = max_mode && g.y == first_row;
+            uint8_t* row = fb + g.y * SCREEN_W;
+            const int xa = g.x0 + lane * 8;
+#pragma unroll
+            for (int j = 0; j < 8; j++) {
+                int xx = xa + j;
+                if (xx < g.x1) {
+                    uint32_t pa = seg_dot_pa(rs, g, xx, nsl, lo, hi);
+                    uint32_t px = rs.pal[pa];
+                    uint8_t val = raw ? (uint8_t)px : FME_LDG(d.lut + px);
+                    if (to_stage) stage[xx] = val;
+                    else if (max_mode) { uint8_t o = row[xx]; row[xx] = val > o ? val : o; }
+                    else row[xx] = val;
+                }
+            }
+        } else if (type == REC_DMA) {
+            if (r + 16 >= nrec) break;  // truncated payload (the frame overflowed its log; status says so)
+            if (lane < 16) {
+                uint4 pl = recs[r + 1 + lane];
+                *reinterpret_cast<uint4*>(rs.oam + 16 * lane) = pl;
+            }
+            r += 16;
+            oam_ver++;
+        } else if (type == REC_VSNAP) {
+            if (r + VRAM_BYTES / 16 >= nrec) break;
+            for (int q = lane; q < VRAM_BYTES / 16; q += 32)
+                reinterpret_cast<uint4*>(rs.vram)[q] = recs[r + 1 + q];
+            r += VRAM_BYTES / 16;
+        } else if (type == REC_LIST) {
+            rs.nsl = (rec.x >> 4) & 0xffu; rs.sl_lo = rec.y; rs.sl_hi = rec.z;
+        } else if (lane == 0) {
+            uint32_t idx = (rec.x >> 4) & 0x7ffu, val = (rec.x >> 16) & 0xffu;
+            if (type == REC_VRAM) rs.vram[idx] = (uint8_t)val;
+            else if (type == REC_PAL) rs.pal[idx & 31u] = (uint8_t)val;
+            else if (type == REC_OAM) rs.oam[idx & 255u] = (uint8_t)val;
+        }
+        if (type == REC_OAM) oam_ver++;
+        __syncwarp();
+    }
+    if (max_mode && first_row >= 0) {
+        uint8_t* row = fb + first_row * SCREEN_W;
+        for (int xx = lane; xx < SCREEN_W; xx += 32) { uint8_t o = row[xx], s = stage[xx]; row[xx] = s > o ? s : o; }
+    }
+    __syncwarp();
+}
+
+// 84x84 area resize of the framebuffer into RS_OBS (warp-wide; lane owns columns lane, lane+32, lane+64)
+__device__ void resize_fb(uint8_t* sm, int lane) {
+    const uint8_t* fb = sm + RS_FB;
+    uint8_t* out = sm + RS_OBS;
+    int32_t xs[3][6];
+    float xw[3][6];
+#pragma unroll
+    for (int q = 0; q < 3; q++) {
+        int dx = lane + 32 * q;
+#pragma unroll
+        for (int k = 0; k < 6; k++) {
+            xs[q][k] = dx < OBS ? c_area.xs[k][dx] : 0;
+            xw[q][k] = dx < OBS ? c_area.xw[k][dx] : 0.f;
+        }
+    }
+    for (int dy = 0; dy < OBS; dy++) {
+        float sacc[3] = {0.f, 0.f, 0.f};
+        for (int m = 0; m < 6; m++) {
+            float wy = c_area.yw[m][dy];
+            if (wy == 0.f) break;
+            const uint8_t* row = fb + c_area.ys[m][dy] * SCREEN_W;
+#pragma unroll
+            for (int q = 0; q < 3; q++) {
+                float b = 0.f;
+#pragma unroll
+                for (int k = 0; k < 6; k++) {
+                    if (xw[q][k] != 0.f) b = fadd(b, fmul((float)row[xs[q][k]], xw[q][k]));
+                }
+                sacc[q] = fadd(sacc[q], fmul(wy, b));
+            }
+        }
+#pragma unroll
+        for (int q = 0; q < 3; q++) {
+            int dx = lane + 32 * q;
+            if (dx < OBS) out[dy * OBS + dx] = sat_round(sacc[q]);
+        }
+    }
+    __syncwarp();
+}
+
+// warp copy helpers (16-byte granules; all buffers here are 16-byte aligned and sized in 16-byte units)
+__device__ __forceinline__ void wcopy16(uint8_t* dst, const uint8_t* src, int nbytes, int lane) {
+    const uint4* s = reinterpret_cast<const uint4*>(src);
+    uint4* d = reinterpret_cast<uint4*>(dst);
+    for (int i = lane; i < nbytes / 16; i += 32) d[i] = s[i];
+}
+__device__ __forceinline__ void wzero16(uint8_t* dst, int nbytes, int lane) {
+    uint4* d = reinterpret_cast<uint4*>(dst);
+    uint4 z = make_uint4(0, 0, 0, 0);
+    for (int i = lane; i < nbytes / 16; i += 32) d[i] = z;
+}
+// thread-private 16-byte copy
+__device__ __forceinline__ void tcopy16(uint8_t* dst, const uint8_t* src, int nbytes) {
+    const uint4* s = reinterpret_cast<const uint4*>(src);
+    uint4* d = reinterpret_cast<uint4*>(dst);
+    for (int i = 0; i < nbytes / 16; i++) d[i] = s[i];
+}
+// forward move inside one buffer (dst < src); safe for overlapping ranges moved by >= 512 bytes
+__device__ __forceinline__ void wmove16(uint8_t* dst, const uint8_t* src, int nbytes, int lane) {
+    const uint4* s = reinterpret_cast<const uint4*>(src);
+    uint4* d = reinterpret_cast<uint4*>(dst);
+    const int n16 = nbytes / 16;
+    for (int base = 0; base < n16; base += 32) {
+        int i = base + lane;
+        uint4 v;
+        if (i < n16) v = s[i];
+        __syncwarp();
+        if (i < n16) d[i] = v;
+    }
+}
+
+}  // namespace fme

@@ -1,0 +1,200 @@
+// fme_render.h - replay of one frame's log into a 240x256 framebuffer, and the 256x240 -> 84x84 area resize.
+//
+// Pixel semantics follow the reference's render path (nes_core.hpp:422-513): background pattern/attribute
+// per dot with the dot's own v (coarse-x increments inside a segment), left-edge hiding, the first opaque
+// sprite of the line's list per dot with its priority bit, palette lookup, then either the palette value
+// (raw screen, nes_core.hpp:503-506) or the cv2 gray value (507-512).
+//
+// Layout of the work: a warp renders one env-frame at a time. Records are read by all lanes (broadcast
+// loads); a segment's dots are split 8 per lane; palette/VRAM/OAM writes and DMA payloads are applied to the
+// warp's shared-memory copies in record order, so every segment sees exactly the contents the PPU saw.
+// When a frame is max-pooled with the previous one, the only row the frame can draw twice (the row of its
+// first segment, because an emulated frame is 1-2 PPU calls longer than a PPU frame) is staged separately so
+// "later write wins" inside the frame and "max" applies only across frames.
+//
+// The area resize reproduces OpenCV's float INTER_AREA in the operation order of the reference's fast
+// resizer (fastmario.cpp:157-201): per source row the horizontal taps are summed from 0.f in tap order,
+// then the vertical taps, no fused multiply-add, round-half-even and saturation.
+#pragma once
+#include "fme_defs.h"
+
+#if defined(__CUDA_ARCH__)
+#define FME_LDG(p) __ldg(p)
+#else
+#ifndef FME_LDG
+#define FME_LDG(p) (*(p))
+#endif
+#endif
+
+namespace fme {
+
+struct AreaTabs {           // per output column / row up to 6 (index, weight) taps, zero-weight padded
+    int32_t xs[6][OBS];
+    float xw[6][OBS];
+    int32_t ys[6][OBS];
+    float yw[6][OBS];
+};
+
+// Render state of the warp (all pointers into shared memory except chr).
+struct RState {
+    uint8_t* vram;   // 2048
+    uint8_t* pal;    // 32
+    uint8_t* oam;    // 256
+    const uint8_t* chr;
+    uint32_t nt[4];
+    // current explicit list (used by segments without a pending evaluation)
+    uint32_t nsl, sl_lo, sl_hi;
+};
+
+FME_HD uint32_t r_pb_read(const RState& s, uint32_t addr) {
+    if (addr < 0x2000) return FME_LDG(s.chr + addr);
+    if (addr < 0x3eff) {
+        uint32_t tsel = addr < 0x2400 ? 0u : addr < 0x2800 ? 1u : addr < 0x2c00 ? 2u : 3u;
+        return s.vram[s.nt[tsel] + (addr & 0x3ffu)];
+    }
+    if (addr < 0x3fff) return s.pal[addr & 0x1fu];
+    return 0;
+}
+
+// segment descriptor decoded once per record
+struct Seg {
+    int y, x0, x1;
+    uint32_t v, fine_x, flags;
+    uint32_t pend, ev_y, oam_addr;
+};
+FME_HD Seg decode_seg(uint4 r) {
+    Seg s;
+    s.y = (int)((r.x >> 4) & 0xffu); s.x0 = (int)((r.x >> 12) & 0x1ffu); s.x1 = (int)((r.x >> 21) & 0x1ffu);
+    s.v = r.y & 0xffffu; s.fine_x = (r.y >> 16) & 7u; s.flags = (r.y >> 19) & 0x7fu;
+    s.pend = r.z & 1u; s.ev_y = (r.z >> 1) & 0xffu; s.oam_addr = (r.z >> 9) & 0xffu;
+    return s;
+}
+
+// v after n coarse-x increments (nes_core.hpp:310-315 applied n times in closed form)
+FME_HD uint32_t v_after(uint32_t v, int n) {
+    if (n <= 0) return v;
+    uint32_t tot = (v & 0x1fu) + (uint32_t)n;
+    uint32_t r = (v & ~0x1fu & 0xffffu) | (tot & 31u);
+    // each wrap of the 5-bit coarse x toggles the nametable bit
+    if (((tot >> 5) & 1u)) r ^= 0x0400u;
+    return r;
+}
+FME_HD int inc_count_fx(uint32_t fine_x, int x0, int x1) {
+    int r = (7 - (int)fine_x) & 7;
+    return (x1 - r + 7) / 8 - (x0 - r + 7) / 8;
+}
+
+// 2-bit sprite pattern (exact integer semantics of nes_core.hpp:368-387) using the segment's flags
+FME_HD uint32_t r_spr_bits(const RState& s, uint32_t flags, int i, int xx, int yy) {
+    int spr_x = (int)s.oam[i * 4 + 3];
+    int spr_y = (int)((s.oam[i * 4 + 0] + 1u) & 0xffu);
+    int tile = (int)s.oam[i * 4 + 1], attribute = (int)s.oam[i * 4 + 2];
+    bool lng = (flags & RF_LONG) != 0;
+    int length = lng ? 16 : 8;
+    int x_shift = (xx - spr_x) % 8, y_offset = (yy - spr_y) % length;
+    if ((attribute & 0x40) == 0) x_shift ^= 7;
+    if ((attribute & 0x80) != 0) y_offset ^= (length - 1);
+    uint32_t address;
+    if (!lng) {
+        address = (uint32_t)(tile * 16 + y_offset) & 0xffffu;
+        if (flags & RF_SPR_PAGE) address = (address + 0x1000u) & 0xffffu;
+    } else {
+        y_offset = (y_offset & 7) | ((y_offset & 8) << 1);
+        address = (uint32_t)((tile >> 1) * 32 + y_offset) & 0xffffu;
+        address |= (uint32_t)(tile & 1) << 12;
+    }
+    uint32_t c = (r_pb_read(s, address) >> x_shift) & 1u;
+    c |= ((r_pb_read(s, (address + 8u) & 0xffffu) >> x_shift) & 1u) << 1;
+    return c;
+}
+
+// sprite list of a segment whose evaluation is still pending (nes_core.hpp:336-349), scalar form
+FME_HD void r_eval_scalar(const RState& s, const Seg& g, uint32_t& nsl, uint32_t& lo, uint32_t& hi) {
+    uint32_t n = 0; lo = 0; hi = 0;
+    int range = (g.flags & RF_LONG) ? 16 : 8;
+    for (int i = (int)(g.oam_addr >> 2); i < 64; ++i) {
+        int diff = (int)g.ev_y - (int)s.oam[i * 4];
+        if (0 <= diff && diff < range) {
+            if (n < 4) lo |= (uint32_t)i << (8 * n); else hi |= (uint32_t)i << (8 * (n - 4));
+            if (++n >= 8) break;
+        }
+    }
+    nsl = n;
+}
+
+// palette address (0..31) of dot x of segment g, with sprite list (nsl, lo, hi)
+FME_HD uint32_t seg_dot_pa(const RState& s, const Seg& g, int xx, uint32_t nsl, uint32_t lo, uint32_t hi) {
+    uint32_t pa = 0;
+    if (g.flags & RF_SHOW_BG) {
+        uint32_t vx = v_after(g.v, inc_count_fx(g.fine_x, g.x0, xx));
+        uint32_t xf = (g.fine_x + (uint32_t)xx) & 7u;
+        uint32_t tile = s.vram[s.nt[((0x2000u | (vx & 0x0fffu)) >> 10) & 3u] + (vx & 0x3ffu)];
+        uint32_t addr = (((tile * 16u) + ((vx >> 12) & 7u)) | ((g.flags & RF_BG_PAGE) ? 0x1000u : 0u)) & 0xffffu;
+        uint32_t b = (FME_LDG(s.chr + (addr & 0x1fffu)) >> (7u ^ xf)) & 1u;
+        b |= ((FME_LDG(s.chr + ((addr + 8u) & 0x1fffu)) >> (7u ^ xf)) & 1u) << 1;
+        if (b) {
+            uint32_t aaddr = 0x23C0u | (vx & 0x0C00u) | ((vx >> 4) & 0x38u) | ((vx >> 2) & 0x07u);
+            uint32_t attr = s.vram[s.nt[(aaddr >> 10) & 3u] + (aaddr & 0x3ffu)];
+            uint32_t shift = ((vx >> 4) & 4u) | (vx & 2u);
+            pa = b | (((attr >> shift) & 3u) << 2);
+        }
+        if ((g.flags & RF_HIDE_BG) && xx < 8) pa = 0;
+    }
+    if ((g.flags & RF_SHOW_SPR) && nsl && !((g.flags & RF_HIDE_SPR) && xx < 8)) {
+        for (uint32_t k = 0; k < nsl; k++) {
+            int i = (int)(((k < 4 ? lo >> (8 * k) : hi >> (8 * (k - 4)))) & 0xffu);
+            int sx = (int)s.oam[i * 4 + 3];
+            if (xx < sx || xx >= sx + 8) continue;
+            uint32_t c = r_spr_bits(s, g.flags, i, xx, g.y);
+            if (!c) continue;
+            uint32_t attribute = s.oam[i * 4 + 2];
+            uint32_t col = c | 0x10u | ((attribute & 3u) << 2);
+            bool front = !(attribute & 0x20u);
+            if (!(pa & 3u) || front) pa = col;
+            break;  // the first opaque sprite of the list decides this dot
+        }
+    }
+    return pa;
+}
+
+// ---------------------------------------------------------------- area resize (portable, one output pixel)
+FME_HD uint8_t sat_round(float v) {
+#if defined(__CUDA_ARCH__)
+    int iv = __float2int_rn(v);
+#else
+    int iv = (int)__builtin_lrintf(v);
+#endif
+    return (uint8_t)(iv < 0 ? 0 : iv > 255 ? 255 : iv);
+}
+FME_HD float fmul(float a, float b) {
+#if defined(__CUDA_ARCH__)
+    return __fmul_rn(a, b);
+#else
+    return a * b;
+#endif
+}
+FME_HD float fadd(float a, float b) {
+#if defined(__CUDA_ARCH__)
+    return __fadd_rn(a, b);
+#else
+    return a + b;
+#endif
+}
+FME_HD uint8_t area_pixel(const uint8_t* fb, const AreaTabs& T, int dy, int dx) {
+    float sacc = 0.f;
+    for (int m = 0; m < 6; m++) {
+        float wy = T.yw[m][dy];
+        if (wy == 0.f) break;
+        const uint8_t* row = fb + T.ys[m][dy] * SCREEN_W;
+        float b = 0.f;
+        for (int k = 0; k < 6; k++) {
+            float wx = T.xw[k][dx];
+            if (wx == 0.f) break;
+            b = fadd(b, fmul((float)row[T.xs[k][dx]], wx));
+        }
+        sacc = fadd(sacc, fmul(wy, b));
+    }
+    return sat_round(sacc);
+}
+
+}  // namespace fme

@@ -1,0 +1,150 @@
+/* fme.h - C ABI of libfme_cuda.so, the B200 batched NES / SMB-style environment engine.
+ *
+ * This is the boundary the Python host code (and any other FFI caller) binds. It replaces the reference's
+ * GPU path, CudaVecEnv -> cujit.Module.launch -> cuLaunchKernel with a by-value StepArgs struct
+ * (src/fast_mario_env/cuda/vec_env.py:197-231, 350-373; cuda/cujit.py:157-178), and mirrors the shape of the
+ * reference's CPU C ABI (csrc/fastmario.cpp:562-674) so a caller of either finds the same concepts:
+ * create -> set_buffers -> reset -> step, plus frames / bad_ops / per-env RAM and the raw console API.
+ *
+ * Conventions
+ *  - Every function returns 0 on success or a negative FME_E* code; no C++ exception crosses the ABI.
+ *    fme_last_error() gives a message for the last failure on the calling thread.
+ *  - Device buffers passed in are owned by the caller (for example torch tensors) and must stay alive
+ *    while the env uses them; the library never frees them.
+ *  - fme_reset / fme_step only enqueue work on the given CUDA stream (cudaStream_t passed as void*;
+ *    NULL = legacy default stream). They do not synchronise and do not allocate.
+ *  - One env object must not be stepped from two threads or two streams at once.
+ *  - Errors detected on the device (log overflow, frame caps, bad actions) are latched into a status word;
+ *    read it with fme_poll_error after synchronising the stream.
+ */
+#ifndef FME_H
+#define FME_H
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define FME_OK 0
+#define FME_E_ARG (-1)       /* invalid argument (sizes, skip outside 1..16, ...) */
+#define FME_E_ROM (-2)       /* ROM rejected (not iNES, mapper != 0, PRG banks not 1..2, CHR banks != 1) */
+#define FME_E_CUDA (-3)      /* a CUDA runtime call failed */
+#define FME_E_DEVICE (-4)    /* a device-side status bit is set (see fme_poll_error) */
+#define FME_E_STATE (-5)     /* call order violated (e.g. step before set_buffers) */
+
+/* device status bits reported by fme_poll_error */
+#define FME_ST_LOG_OVERFLOW 1u   /* a frame produced more PPU log records than log_capacity */
+#define FME_ST_HACK_CAP 2u       /* the busy-state skip loop hit its frame cap (reference would spin) */
+#define FME_ST_BOOT_CAP 4u       /* level boot hit its frame cap (reference would spin) */
+#define FME_ST_BAD_ACTION 8u     /* an action outside 0..6 was given (treated as 0) */
+
+typedef struct FmeEnv FmeEnv;
+typedef struct FmeRaw FmeRaw;
+
+/* Env configuration; field meanings follow FastVecEnv / CudaVecEnv (src/fast_mario_env/env.py:140-142,
+ * cuda/vec_env.py:247-249) and fm_create (csrc/fastmario.cpp:566-568). */
+typedef struct FmeConfig {
+    int32_t n_envs;
+    int32_t skip;          /* NES frames per agent step, 1..16 */
+    int32_t max_steps;     /* time limit in agent steps */
+    int32_t noop_max;      /* 0 disables random no-op starts */
+    int32_t maxpool;       /* max over the gray frames of the last two frame-steps */
+    int32_t frame_stack;   /* k >= 1 */
+    double sticky;         /* probability of repeating the previous action, per NES frame */
+    int32_t device;        /* CUDA device ordinal */
+    int32_t log_capacity;  /* PPU log records per frame slot; 0 = default (2048) */
+    int32_t hack_cap;      /* frame cap for one busy-state skip loop; 0 = default (20000) */
+    int32_t boot_cap;      /* frame cap for booting one level; 0 = default (20000) */
+} FmeConfig;
+
+/* Output buffers (device pointers). Shapes as CudaVecEnv's (cuda/vec_env.py:316-328):
+ * obs/final_obs uint8 (N, k, 84, 84); rew float32 (N,); term/trunc uint8 (N,); info int32 (N, 10) in the
+ * order x_pos, flag_get, life, score, time, world, stage, coins, y_pos, status; ep_ret float64 (N,);
+ * ep_len int32 (N,). final_obs / ep_ret / ep_len are written only for envs whose episode ended. */
+typedef struct FmeBuffers {
+    uint8_t* obs;
+    uint8_t* final_obs;
+    float* rew;
+    uint8_t* term;
+    uint8_t* trunc;
+    int32_t* info;
+    double* ep_ret;
+    int32_t* ep_len;
+} FmeBuffers;
+
+/* Create N envs. Replaces fm_create (csrc/fastmario.cpp:566-601) and CudaVecEnv.__init__
+ * (cuda/vec_env.py:247-347): validates the ROM (fm_create returns NULL on a bad ROM or skip), boots each
+ * distinct level on the GPU and builds the per-(level, k) no-op reset cache.
+ *   rom, rom_len   iNES image
+ *   levels         N x 3 int32 (world, stage, area) as decode_level returns (rom.py:88-103)
+ *   gray_lut       256 bytes, palette value -> gray (env.py:42-47)
+ *   rng            N x 6 uint64: state_hi, state_lo, inc_hi, inc_lo, has_uint32, uinteger of
+ *                  numpy default_rng(seed*1000 + env_offset + i) (env.py:50-55, 155-156)
+ * Synchronises the device once at the end (boot and cache construction). */
+int fme_create(const FmeConfig* cfg, const uint8_t* rom, int64_t rom_len, const int32_t* levels,
+               const uint8_t* gray_lut, const uint64_t* rng, FmeEnv** out);
+
+/* Bind caller-owned device output buffers. Replaces fm_set_buffers (csrc/fastmario.cpp:603-608). */
+int fme_set_buffers(FmeEnv* env, const FmeBuffers* bufs);
+
+/* Reset every env (random no-op start from the reset cache), write the zero-padded frame stacks.
+ * Replaces fm_reset (csrc/fastmario.cpp:610) / CudaVecEnv.reset (cuda/vec_env.py:363-365). Async. */
+int fme_reset(FmeEnv* env, void* stream);
+
+/* One agent step for every env; d_actions is int64 (N,) on the device (0..6, SIMPLE_MOVEMENT index).
+ * Replaces fm_step_async + fm_step_wait (csrc/fastmario.cpp:611-617) and CudaVecEnv.step
+ * (cuda/vec_env.py:367-373): sticky actions, frame skip, max-pool, reward/done/info, busy-state skipping,
+ * time limit, frame stack, final_obs and auto-reset. Async; enqueues only. */
+int fme_step(FmeEnv* env, const int64_t* d_actions, void* stream);
+
+/* OR of the device status bits of all envs since create (call after synchronising). */
+int fme_poll_error(FmeEnv* env, uint32_t* status);
+
+/* Copy env i's 2 KB RAM to host memory (synchronous). Replaces fm_env_ram (csrc/fastmario.cpp:630). */
+int fme_env_ram(FmeEnv* env, int32_t i, uint8_t* host_out);
+/* All envs' RAM as (N, 2048) uint8 into a device buffer, async. Replaces CudaVecEnv.ram (vec_env.py:375-378). */
+int fme_ram_all(FmeEnv* env, uint8_t* d_out, void* stream);
+
+/* Total emulated NES frames and unimplemented opcodes over all envs (synchronous).
+ * Replace fm_frames / fm_bad_ops (csrc/fastmario.cpp:619-628). */
+int fme_frames(FmeEnv* env, int64_t* out);
+int fme_bad_ops(FmeEnv* env, int64_t* out);
+/* Device bytes held per env (replaces fm_env_bytes, csrc/fastmario.cpp:632-635). */
+int64_t fme_env_bytes(FmeEnv* env);
+
+/* Destroy and free the library-owned device memory. Replaces fm_destroy (csrc/fastmario.cpp:618). */
+void fme_destroy(FmeEnv* env);
+
+/* ---- raw consoles (frame-level fidelity), replacing fm_raw_* (csrc/fastmario.cpp:651-673) ---- */
+/* n independent consoles powered on from the same ROM. */
+int fme_raw_create(const uint8_t* rom, int64_t rom_len, int32_t n, int32_t device, int32_t log_capacity,
+                   FmeRaw** out);
+/* One NES frame for every console: d_buttons uint8 (n,) device; render != 0 also writes the 240x256
+ * palette-value screens (as fm_raw_frame with render=1 fills fm_raw_screen). Async. */
+int fme_raw_frame(FmeRaw* raw, const uint8_t* d_buttons, int32_t render, void* stream);
+/* RAM (n, 2048) and screens (n, 240, 256) into device buffers, async. */
+int fme_raw_ram(FmeRaw* raw, uint8_t* d_out, void* stream);
+int fme_raw_screen(FmeRaw* raw, uint8_t* d_out, void* stream);
+/* Snapshot / restore every console (fm_raw_backup / fm_raw_restore). Async. */
+int fme_raw_backup(FmeRaw* raw, void* stream);
+int fme_raw_restore(FmeRaw* raw, void* stream);
+int fme_raw_bad_ops(FmeRaw* raw, int64_t* out);
+int fme_raw_poll_error(FmeRaw* raw, uint32_t* status);
+void fme_raw_destroy(FmeRaw* raw);
+
+/* ---- helpers ---- */
+/* nes-py master palette, 64 x 0xRRGGBB (replaces fm_palette, csrc/fastmario.cpp:637). */
+void fme_palette(uint32_t* out64);
+/* 240x256 gray -> 84x84 INTER_AREA on the device, n images, async (replaces fm_resize_fast,
+ * csrc/fastmario.cpp:643-649, with the same float operation order). */
+int fme_resize(const uint8_t* d_src, uint8_t* d_dst, int32_t n, void* stream);
+/* Console state size in bytes of the reset-cache image (cf. fm_state_bytes, csrc/fastmario.cpp:631). */
+int64_t fme_state_bytes(void);
+const char* fme_last_error(void);
+const char* fme_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* FME_H */

@@ -1,0 +1,97 @@
+"""GPU API behaviour: shapes/dtypes, zero-padded stacks, determinism, env_offset sharding, the FastVecEnv
+wrapper, the device resize, and device-side error reporting (the reference's tests/test_api.py pattern)."""
+import os
+
+import numpy as np
+import pytest
+from conftest import fme
+
+pytestmark = pytest.mark.gpu
+GOLD = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
+
+
+def test_shapes_and_infos(rom):
+    v = fme.FastVecEnv("1-1", 3, seed=0, max_steps=20, rom=rom)
+    obs = v.reset()
+    assert obs.shape == (3, 4, 84, 84) and obs.dtype == np.uint8
+    assert (obs[:, :3] == 0).all() and obs[:, 3].any()
+    ended = 0
+    for t in range(25):
+        obs, r, te, tr, infos = v.step(np.full(3, 1))
+        assert r.dtype == np.float32 and te.dtype == bool and tr.dtype == bool and len(infos) == 3
+        assert set(fme.INFO_KEYS) <= set(infos[0])
+        for i in np.flatnonzero(te | tr):
+            ended += 1
+            assert infos[i]["final_obs"].shape == (4, 84, 84)
+            assert infos[i]["episode"]["l"] == 20 and infos[i]["TimeLimit.truncated"]
+    assert ended == 3
+    assert v.bad_ops() == 0 and v.frames > 0
+    v.check()
+    v.close()
+
+
+def test_determinism(rom):
+    import torch
+    acts = torch.from_numpy(np.random.default_rng(0).integers(0, 7, (40, 64))).cuda()
+    outs = []
+    for _ in range(2):
+        e = fme.CudaVecEnv(["1-1", "1-2", "4-1", "8-4"] * 16, 64, seed=5, sticky=0.25, noop_max=10, maxpool=True, rom=rom)
+        o = [e.reset().clone()]
+        for a in acts:
+            o.append(e.step(a)[0].clone())
+        outs.append(torch.stack(o))
+        e.close()
+    assert torch.equal(outs[0], outs[1])
+
+
+def test_env_offset_matches_slice(rom):
+    import torch
+    acts = torch.from_numpy(np.random.default_rng(1).integers(0, 7, (30, 48))).cuda()
+    a = fme.CudaVecEnv("1-1", 48, seed=2, sticky=0.25, noop_max=10, rom=rom)
+    b = fme.CudaVecEnv("1-1", 16, seed=2, sticky=0.25, noop_max=10, env_offset=32, rom=rom)
+    oa, ob = a.reset(), b.reset()
+    assert torch.equal(oa[32:], ob)
+    for x in acts:
+        oa, ob = a.step(x)[0], b.step(x[32:].contiguous())[0]
+        assert torch.equal(oa[32:], ob)
+
+
+def test_fastvecenv_matches_cudavecenv(rom):
+    import torch
+    kw = dict(seed=3, sticky=0.25, noop_max=30, maxpool=True, max_steps=50, rom=rom)
+    f = fme.FastVecEnv("1-1", 8, **kw)
+    c = fme.CudaVecEnv("1-1", 8, **kw)
+    assert np.array_equal(f.reset(), c.reset().cpu().numpy())
+    rng = np.random.default_rng(4)
+    for _ in range(60):
+        a = rng.integers(0, 7, 8)
+        o1, r1, te1, tr1, infos = f.step(a)
+        o2, r2, te2, tr2, i2 = c.step(torch.from_numpy(a).cuda())
+        assert np.array_equal(o1, o2.cpu().numpy()) and np.array_equal(r1, r2.cpu().numpy())
+        assert np.array_equal(te1, te2.cpu().numpy()) and np.array_equal(tr1, tr2.cpu().numpy())
+        for i in range(8):
+            assert infos[i]["x_pos"] == int(i2["x_pos"][i])
+
+
+def test_resize_matches_cv2_golden():
+    g = np.load(os.path.join(GOLD, "resize.npz"))
+    out = fme.resize_area(g["src"])
+    assert np.array_equal(out, g["dst"])
+
+
+def test_bad_action_is_reported(rom):
+    import torch
+    e = fme.CudaVecEnv("1-1", 4, rom=rom)
+    e.reset()
+    e.step(torch.tensor([0, 1, 9, 2], device="cuda"))
+    with pytest.raises(Exception, match="action"):
+        e.check()
+
+
+def test_log_overflow_is_reported_not_silent(rom):
+    import torch
+    e = fme.CudaVecEnv("1-1", 4, rom=rom, log_capacity=64)
+    e.reset()
+    e.step(torch.zeros(4, dtype=torch.int64, device="cuda"))
+    with pytest.raises(Exception, match="log"):
+        e.check()

@@ -244,7 +244,7 @@ def main():
         if dist:
             dist.all_reduce(dt_t, op=dist.ReduceOp.MAX)
         h2d = E * 8
-        d2h = E * (4 * 84 * 84 * 2 + 4 + 1 + 1 + 40 + 8 + 4)
+        d2h = E * (4 * 84 * 84 + 4 + 1 + 1 + 40 + 8 + 4)  # + final_obs rows of the envs that ended
         e2e = {"value": world * E * args.steps / float(dt_t.item()), "unit": UNIT, "h2d_bytes_per_step": h2d * world,
                "d2h_bytes_per_step": d2h * world, "api": "FastVecEnv.step (numpy in/out, full stacks, infos)"}
         fenv.close()

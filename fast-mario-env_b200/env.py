@@ -237,7 +237,6 @@ class FastVecEnv:
         pin = dict(pin_memory=True)
         self._act = torch.zeros(n_envs, dtype=torch.int64, **pin)
         self._obs = torch.zeros(n_envs, frame_stack, OBS_HW, OBS_HW, dtype=torch.uint8, **pin)
-        self._fin = torch.zeros_like(self._obs, **pin)
         self._rew = torch.zeros(n_envs, dtype=torch.float32, **pin)
         self._term = torch.zeros(n_envs, dtype=torch.bool, **pin)
         self._trunc = torch.zeros(n_envs, dtype=torch.bool, **pin)
@@ -279,7 +278,7 @@ class FastVecEnv:
         self.env.step(self.env.actions)
         e = self.env
         for dst, src in ((self._obs, e.obs), (self._rew, e.rew), (self._term, e.term), (self._trunc, e.trunc),
-                         (self._info, e.info_t), (self._epr, e.ep_ret), (self._epl, e.ep_len), (self._fin, e.final_obs)):
+                         (self._info, e.info_t), (self._epr, e.ep_ret), (self._epl, e.ep_len)):
             dst.copy_(src, non_blocking=True)
         self._event.record()
         self._pending = True
@@ -291,14 +290,20 @@ class FastVecEnv:
         term = self._term.numpy().copy()
         trunc = self._trunc.numpy().copy()
         inf = self._info.numpy().tolist()
-        fin, epr, epl = self._fin.numpy(), self._epr.numpy(), self._epl.numpy()
+        ended = np.flatnonzero(term | trunc)
+        fin = {}
+        if len(ended):  # final_obs only for the envs whose episode ended (usually a small fraction)
+            idx = _torch().from_numpy(ended).to(self.env.dev)
+            rows = self.env.final_obs.index_select(0, idx).cpu().numpy()
+            fin = {int(i): rows[k] for k, i in enumerate(ended)}
+        epr, epl = self._epr.numpy(), self._epl.numpy()
         infos = []
         for i in range(self.n):
             r = inf[i]
             info = {"x_pos": r[0], "flag_get": bool(r[1]), "life": r[2], "score": r[3], "time": r[4],
                     "world": r[5], "stage": r[6]}
             if term[i] or trunc[i]:
-                info["final_obs"] = fin[i].copy()
+                info["final_obs"] = fin[i]
                 info["TimeLimit.truncated"] = bool(trunc[i] and not term[i])
                 ep = dict(r=round(float(epr[i]), 6), l=int(epl[i]), t=round(time.time() - self.t0, 6),
                           x_pos=info["x_pos"], flag_get=info["flag_get"])

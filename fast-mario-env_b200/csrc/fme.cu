@@ -60,7 +60,7 @@ __global__ void __launch_bounds__(32) k_boot(BootParams P) {
     // phase 0 fa(8), 1 fa(0), then loop A {2: fa(8); write level; 3: fa(0); $7A0=0} while time==0,
     // then loop B {4: fa(8), 5: fa(0)} while time >= tl.
     while (__any_sync(FULL, running)) {
-        if (running) {
+        if (minpc_turn(running, c)) {
             if (!c.step_once()) {
                 c.end_frame();
                 close_frame(c, slot);
@@ -95,6 +95,7 @@ __global__ void __launch_bounds__(32) k_boot(BootParams P) {
         if (c.status) atomicOr(d.err, c.status);
     }
     __syncwarp();
+    load_lut(sm, d.lut, lane);
     for (int j = 0; j < 32; j++) {
         int lj = g * 32 + j;
         if (lj >= P.n_levels) break;
@@ -156,7 +157,7 @@ __global__ void __launch_bounds__(32) k_step(StepParams P) {
     if (active) ag.start(c, ev, cfg, act, d.logs + slot_off(e, 0, cap), d.logs + slot_off(e, 1, cap));
     // one emulated instruction per lane per iteration; the vote keeps the warp converged at the loop head
     while (__any_sync(FULL, running)) {
-        if (running && !c.step_once()) {
+        if (minpc_turn(running, c) && !c.step_once()) {
             c.end_frame();
             running = ag.on_frame_end(c, ev, cfg);
         }
@@ -218,6 +219,7 @@ __global__ void __launch_bounds__(32) k_step(StepParams P) {
     __syncwarp();
 
     // ---- render, resize, frame stack (warp-cooperative, one env at a time)
+    load_lut(sm, d.lut, lane);
     const uint32_t summary = (active ? 1u : 0u) | (pooled ? 2u : 0u) | ((uint32_t)cur_slot << 2) | (ended ? 8u : 0u);
     const int K = P.frame_stack;
     for (int j = 0; j < 32; j++) {
@@ -358,7 +360,7 @@ __global__ void __launch_bounds__(32) k_raw(RawParams P) {
     bool running = active;
     if (active) begin_frame(c, slot, P.buttons[e], d.log_cap);
     while (__any_sync(FULL, running)) {
-        if (running && !c.step_once()) {
+        if (minpc_turn(running, c) && !c.step_once()) {
             c.end_frame();
             close_frame(c, slot);
             running = false;
@@ -375,6 +377,7 @@ __global__ void __launch_bounds__(32) k_raw(RawParams P) {
     copy_slab(d.slab + (size_t)g * SLAB_BYTES, sm, lane);
     __syncwarp();
     if (!P.render) return;
+    load_lut(sm, d.lut, lane);
     for (int j = 0; j < 32; j++) {
         int ej = g * 32 + j;
         if (ej >= d.n) break;

@@ -710,10 +710,9 @@ struct Core {
             default: setf(F_D, true); break;  // SED
         }
     }
-    // one instruction; returns the reference's skip-cycle count
-    FME_HD int32_t execute() {
+    // one instruction whose opcode byte was already read from `pc`; returns the reference's skip-cycle count
+    FME_HD int32_t execute_op(uint32_t opc) {
         skip = 0;
-        uint32_t opc = rd(pc);
         pc = (pc + 1) & 0xffffu;
         uint32_t d = FME_DTAB(opc);
         uint32_t kind = d_kind(d);
@@ -770,6 +769,8 @@ struct Core {
     // ================================================================ frame driver (nes_core.hpp:1166-1204)
     // Run until the instruction boundary test. Returns false once exec_at reached the frame end.
     // One call = one executed instruction (or an NMI / idle-loop skip).
+    // byte at a for the idle-loop test: PRG, or 0xff outside it (rd_prg_fast, nes_core.hpp:153)
+    FME_HD uint32_t prg_fast(uint32_t a) const { a &= 0xffffu; return a >= 0x8000u ? prg(a) : 0xffu; }
     FME_HD bool step_once() {
         if (exec_at >= FRAME_ITERS) return false;
         const int32_t J = exec_at;
@@ -778,7 +779,9 @@ struct Core {
             sync_to(3 * (J + 1));
             if (exec_at != J) return true;  // an NMI was taken before this instruction
         }
-        if (pc >= 0x8000u && pc <= 0xfffdu && prg(pc) == 0x4Cu && (prg(pc + 1) | (prg(pc + 2) << 8)) == pc) {
+        // the opcode byte: PRG reads have no side effects, so it is read once for the idle test and execution
+        const uint32_t opc = pc >= 0x8000u ? prg(pc) : 0x100u;
+        if (opc == 0x4Cu && (prg_fast(pc + 1) | (prg_fast(pc + 2) << 8)) == pc) {
             int32_t lim_end = FRAME_ITERS - J;
             int32_t lim_nmi = nmi_thresh - 3 * (J + 1);
             int32_t k1 = lim_end > 0 ? (lim_end + 2) / 3 : 0;
@@ -791,7 +794,7 @@ struct Core {
             }
         }
         cur = J;
-        int32_t S = execute();
+        int32_t S = execute_op(opc != 0x100u ? opc : rd(pc));
         exec_at = J + (S >= 1 ? S : 1);
         zero_skip = S <= 0;
         return true;

@@ -72,6 +72,17 @@ __device__ __forceinline__ void bind_core(Core& c, const Dev& d, uint8_t* sm, in
     c.vram_burst = 0; c.vram_dirty = false;
 }
 
+// Warp scheduling of the emulation loop: among the lanes that are about to execute an instruction only those
+// at the warp's minimum PC run it, so lanes that took a shorter path wait at the join point and the warp
+// re-converges on identical instructions (results cannot depend on the schedule: lanes are independent).
+// Lanes at a frame boundary always proceed. Returns true if this lane may step now.
+__device__ __forceinline__ bool minpc_turn(bool running, const Core& c) {
+    const bool exec = running && c.exec_at < FRAME_ITERS;
+    const uint32_t key = exec ? c.pc : 0xffffffffu;
+    const uint32_t mn = __reduce_min_sync(FULL, key);
+    return running && (!exec || key == mn);
+}
+
 // coalesced copy of a whole slab between HBM and shared memory (warp-wide)
 __device__ __forceinline__ void copy_slab(uint8_t* dst, const uint8_t* src, int lane) {
     const uint4* s = reinterpret_cast<const uint4*>(src);
@@ -88,17 +99,22 @@ constexpr int RS_PAL = RS_VRAM + VRAM_BYTES;
 constexpr int RS_OAM = RS_PAL + PAL_BYTES;
 constexpr int RS_STAGE = RS_OAM + OAM_BYTES;     // one staged row (256)
 constexpr int RS_OBS = RS_STAGE + SCREEN_W;      // 84 x 84 result
-constexpr int RS_END = RS_OBS + OBS_BYTES;
+constexpr int RS_LUT = RS_OBS + OBS_BYTES;       // 256-entry gray LUT (identity for raw screens)
+constexpr int RS_SPR = RS_LUT + 256;             // 16 words: sprite rows and infos of the current line
+constexpr int RS_END = RS_SPR + 64;
 static_assert(RS_END <= SLAB_BYTES, "render scratch must fit the slab region");
 
 // Replay one logged frame into the framebuffer. raw: palette values (screen) instead of gray.
 // max_mode: combine with the frame already in the framebuffer by max (ALE-style max-pool).
+// Work split: every record is read by all lanes; a segment's dots go 8 per lane (lane L: x0 + 8L ..);
+// the line's sprite rows are fetched once per line by lanes 0..7 and broadcast with shuffles.
 __device__ void render_slot(const uint8_t* slot, uint8_t* sm, const Dev& d, bool raw, bool max_mode, int lane) {
     uint8_t* fb = sm + RS_FB;
     RState rs;
     rs.vram = sm + RS_VRAM; rs.pal = sm + RS_PAL; rs.oam = sm + RS_OAM; rs.chr = d.chr;
     for (int i = 0; i < 4; i++) rs.nt[i] = d.nt[i];
     uint8_t* stage = sm + RS_STAGE;
+    const uint8_t* lut = sm + RS_LUT;
     {
         const uint4* hv = reinterpret_cast<const uint4*>(slot + SLOT_HDR_VRAM);
         uint4* sv = reinterpret_cast<uint4*>(rs.vram);
@@ -114,8 +130,11 @@ __device__ void render_slot(const uint8_t* slot, uint8_t* sm, const Dev& d, bool
     const uint4* recs = reinterpret_cast<const uint4*>(slot + SLOT_HDR_BYTES);
     __syncwarp();
     int first_row = -1;
-    uint32_t lkey = 0xffffffffu, lnsl = 0, llo = 0, lhi = 0;
-    uint32_t oam_ver = 0;
+    uint32_t ver = 0;                                   // bumps on every content change (VRAM/palette/OAM)
+    uint32_t lkey = 0xffffffffu, lnsl = 0, llo = 0, lhi = 0;   // cached pending-evaluation result
+    uint32_t skey0 = 0xffffffffu, skey1 = 0, skey2 = 0;        // cached sprite rows of the current line
+    uint32_t* srow_s = reinterpret_cast<uint32_t*>(sm + RS_SPR);   // the line's sprite rows (list order)
+    uint32_t* sinfo_s = srow_s + 8;
     for (int r = 0; r < nrec; r++) {
         uint4 rec = recs[r];
         uint32_t type = rec.x & 15u;
@@ -123,7 +142,7 @@ __device__ void render_slot(const uint8_t* slot, uint8_t* sm, const Dev& d, bool
             Seg g = decode_seg(rec);
             uint32_t nsl, lo, hi;
             if (g.pend) {
-                uint32_t key = g.ev_y | (g.oam_addr << 8) | ((g.flags & RF_LONG) ? 0x10000u : 0u) | (oam_ver << 17);
+                uint32_t key = g.ev_y | (g.oam_addr << 8) | ((g.flags & RF_LONG) ? 0x10000u : 0u) | (ver << 17);
                 if (key != lkey) {
                     int start = (int)(g.oam_addr >> 2);
                     int range = (g.flags & RF_LONG) ? 16 : 8;
@@ -145,20 +164,41 @@ __device__ void render_slot(const uint8_t* slot, uint8_t* sm, const Dev& d, bool
             } else {
                 nsl = rs.nsl; lo = rs.sl_lo; hi = rs.sl_hi;
             }
+            const bool spr_on = (g.flags & RF_SHOW_SPR) && nsl;
+            if (spr_on) {
+                uint32_t k0 = (uint32_t)g.y | (nsl << 8) | ((g.flags & (RF_LONG | RF_SPR_PAGE)) << 12) | (ver << 20);
+                if (k0 != skey0 || lo != skey1 || hi != skey2) {
+                    if ((uint32_t)lane < nsl) {
+                        int i = (int)(((lane < 4 ? lo >> (8 * lane) : hi >> (8 * (lane - 4)))) & 0xffu);
+                        srow_s[lane] = sprite_row(rs, g.flags, i, g.y);
+                        sinfo_s[lane] = sprite_info(rs, i);
+                    }
+                    skey0 = k0; skey1 = lo; skey2 = hi;
+                    __syncwarp();
+                }
+            }
             if (max_mode && first_row < 0) first_row = g.y;
             const bool to_stage = max_mode && g.y == first_row;
-            uint8_t* row = fb + g.y * SCREEN_W;
             const int xa = g.x0 + lane * 8;
+            uint32_t outw[2];
+            render8(rs, g, xa, spr_on ? nsl : 0u, srow_s, sinfo_s, lut, raw, outw);
+            uint8_t* row = to_stage ? stage : fb + g.y * SCREEN_W;
+            if (xa < g.x1) {
+                if (xa + 8 <= g.x1 && (xa & 7) == 0) {
+                    uint2* dst = reinterpret_cast<uint2*>(row + xa);
+                    uint2 nv = make_uint2(outw[0], outw[1]);
+                    if (max_mode && !to_stage) { uint2 ov = *dst; nv.x = __vmaxu4(nv.x, ov.x); nv.y = __vmaxu4(nv.y, ov.y); }
+                    *dst = nv;
+                } else {
 #pragma unroll
-            for (int j = 0; j < 8; j++) {
-                int xx = xa + j;
-                if (xx < g.x1) {
-                    uint32_t pa = seg_dot_pa(rs, g, xx, nsl, lo, hi);
-                    uint32_t px = rs.pal[pa];
-                    uint8_t val = raw ? (uint8_t)px : FME_LDG(d.lut + px);
-                    if (to_stage) stage[xx] = val;
-                    else if (max_mode) { uint8_t o = row[xx]; row[xx] = val > o ? val : o; }
-                    else row[xx] = val;
+                    for (int j = 0; j < 8; j++) {
+                        const int xx = xa + j;
+                        if (xx < g.x1) {
+                            uint8_t val = (uint8_t)(outw[j >> 2] >> (8 * (j & 3)));
+                            if (max_mode && !to_stage) { uint8_t o = row[xx]; row[xx] = val > o ? val : o; }
+                            else row[xx] = val;
+                        }
+                    }
                 }
             }
         } else if (type == REC_DMA) {
@@ -168,26 +208,29 @@ __device__ void render_slot(const uint8_t* slot, uint8_t* sm, const Dev& d, bool
                 *reinterpret_cast<uint4*>(rs.oam + 16 * lane) = pl;
             }
             r += 16;
-            oam_ver++;
+            ver++;
         } else if (type == REC_VSNAP) {
             if (r + VRAM_BYTES / 16 >= nrec) break;
             for (int q = lane; q < VRAM_BYTES / 16; q += 32)
                 reinterpret_cast<uint4*>(rs.vram)[q] = recs[r + 1 + q];
             r += VRAM_BYTES / 16;
+            ver++;
         } else if (type == REC_LIST) {
             rs.nsl = (rec.x >> 4) & 0xffu; rs.sl_lo = rec.y; rs.sl_hi = rec.z;
-        } else if (lane == 0) {
-            uint32_t idx = (rec.x >> 4) & 0x7ffu, val = (rec.x >> 16) & 0xffu;
-            if (type == REC_VRAM) rs.vram[idx] = (uint8_t)val;
-            else if (type == REC_PAL) rs.pal[idx & 31u] = (uint8_t)val;
-            else if (type == REC_OAM) rs.oam[idx & 255u] = (uint8_t)val;
+        } else {
+            if (lane == 0) {
+                uint32_t idx = (rec.x >> 4) & 0x7ffu, val = (rec.x >> 16) & 0xffu;
+                if (type == REC_VRAM) rs.vram[idx] = (uint8_t)val;
+                else if (type == REC_PAL) rs.pal[idx & 31u] = (uint8_t)val;
+                else if (type == REC_OAM) rs.oam[idx & 255u] = (uint8_t)val;
+            }
+            ver++;
         }
-        if (type == REC_OAM) oam_ver++;
         __syncwarp();
     }
     if (max_mode && first_row >= 0) {
         uint8_t* row = fb + first_row * SCREEN_W;
-        for (int xx = lane; xx < SCREEN_W; xx += 32) { uint8_t o = row[xx], s = stage[xx]; row[xx] = s > o ? s : o; }
+        for (int xx = lane; xx < SCREEN_W; xx += 32) { uint8_t o = row[xx], st = stage[xx]; row[xx] = st > o ? st : o; }
     }
     __syncwarp();
 }
@@ -229,6 +272,12 @@ __device__ void resize_fb(uint8_t* sm, int lane) {
             if (dx < OBS) out[dy * OBS + dx] = sat_round(sacc[q]);
         }
     }
+    __syncwarp();
+}
+
+// gray LUT (or identity) into shared memory before a render phase
+__device__ __forceinline__ void load_lut(uint8_t* sm, const uint8_t* lut, int lane) {
+    if (lane < 16) reinterpret_cast<uint4*>(sm + RS_LUT)[lane] = reinterpret_cast<const uint4*>(lut)[lane];
     __syncwarp();
 }
 

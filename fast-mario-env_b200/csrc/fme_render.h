@@ -197,4 +197,110 @@ FME_HD uint8_t area_pixel(const uint8_t* fb, const AreaTabs& T, int dy, int dx) 
     return sat_round(sacc);
 }
 
+// ---------------------------------------------------------------- 8-dot span form used by the renderers
+FME_HD uint32_t brev8(uint32_t b) {
+#if defined(__CUDA_ARCH__)
+    return __brev(b) >> 24;
+#else
+    b = ((b & 0xF0u) >> 4) | ((b & 0x0Fu) << 4);
+    b = ((b & 0xCCu) >> 2) | ((b & 0x33u) << 2);
+    return ((b & 0xAAu) >> 1) | ((b & 0x55u) << 1);
+#endif
+}
+
+// Row of sprite i on line y as MSB-first pattern bytes (column 0 = bit 7), with the exact address arithmetic
+// of nes_core.hpp:368-387 (negative line offsets of stale lists included). Packed: lo | hi<<8.
+FME_HD uint32_t sprite_row(const RState& rs, uint32_t flags, int i, int y) {
+    int spr_y = (int)((rs.oam[i * 4 + 0] + 1u) & 0xffu);
+    int tile = (int)rs.oam[i * 4 + 1], attribute = (int)rs.oam[i * 4 + 2];
+    bool lng = (flags & RF_LONG) != 0;
+    int length = lng ? 16 : 8;
+    int y_offset = (y - spr_y) % length;
+    if ((attribute & 0x80) != 0) y_offset ^= (length - 1);
+    uint32_t address;
+    if (!lng) {
+        address = (uint32_t)(tile * 16 + y_offset) & 0xffffu;
+        if (flags & RF_SPR_PAGE) address = (address + 0x1000u) & 0xffffu;
+    } else {
+        y_offset = (y_offset & 7) | ((y_offset & 8) << 1);
+        address = (uint32_t)((tile >> 1) * 32 + y_offset) & 0xffffu;
+        address |= (uint32_t)(tile & 1) << 12;
+    }
+    uint32_t lo = r_pb_read(rs, address), hi = r_pb_read(rs, (address + 8u) & 0xffffu);
+    if (attribute & 0x40) { lo = brev8(lo); hi = brev8(hi); }
+    return lo | (hi << 8);
+}
+// x | (0x10 | palette<<2) << 8 | front << 13 of sprite i (the part of nes_core.hpp:426-429 that is per sprite)
+FME_HD uint32_t sprite_info(const RState& rs, int i) {
+    uint32_t attribute = rs.oam[i * 4 + 2];
+    return rs.oam[i * 4 + 3] | ((0x10u | ((attribute & 3u) << 2)) << 8) | ((attribute & 0x20u) ? 0u : (1u << 13));
+}
+
+// background tile of v: pattern bytes (MSB = leftmost dot) and the 2 palette-select bits (nes_core.hpp:453-464)
+FME_HD void bg_tile(const RState& rs, uint32_t v, uint32_t bg_page, uint32_t& lo, uint32_t& hi, uint32_t& at) {
+    uint32_t tile = rs.vram[rs.nt[(v >> 10) & 3u] + (v & 0x3ffu)];
+    uint32_t addr = ((tile * 16u) + ((v >> 12) & 7u)) | (bg_page << 12);
+    lo = FME_LDG(rs.chr + (addr & 0x1fffu));
+    hi = FME_LDG(rs.chr + ((addr + 8u) & 0x1fffu));
+    uint32_t aaddr = 0x23C0u | (v & 0x0C00u) | ((v >> 4) & 0x38u) | ((v >> 2) & 0x07u);
+    uint32_t attr = rs.vram[rs.nt[(aaddr >> 10) & 3u] + (aaddr & 0x3ffu)];
+    at = (attr >> (((v >> 4) & 4u) | (v & 2u))) & 3u;
+}
+
+// The 8 output values of dots xa..xa+7 of segment g (bytes j of out[0..1]; dots outside the segment are
+// computed but must not be stored). srow/sinfo: the line's sprite rows (list order), nsl of them.
+FME_HD void render8(const RState& rs, const Seg& g, int xa, uint32_t nsl, const uint32_t* srow, const uint32_t* sinfo,
+                    const uint8_t* lut, bool raw, uint32_t* out) {
+    uint32_t wlo = 0, whi = 0, at0 = 0, at1 = 0, s = 0;
+    if (g.flags & RF_SHOW_BG) {
+        const int tx0 = ((int)g.fine_x + g.x0) >> 3;
+        const int t0 = ((int)g.fine_x + xa) >> 3;
+        s = ((uint32_t)g.fine_x + (uint32_t)xa) & 7u;
+        const uint32_t bgp = (g.flags & RF_BG_PAGE) ? 1u : 0u;
+        uint32_t lo0, hi0, lo1 = 0, hi1 = 0;
+        bg_tile(rs, v_after(g.v, t0 - tx0), bgp, lo0, hi0, at0);
+        at1 = at0;
+        if (s) bg_tile(rs, v_after(g.v, t0 + 1 - tx0), bgp, lo1, hi1, at1);
+        wlo = (((lo0 << 8) | lo1) >> (8u - s)) & 0xffu;
+        whi = (((hi0 << 8) | hi1) >> (8u - s)) & 0xffu;
+    }
+    uint32_t filled = 0, front_m = 0, sc0 = 0, sc1 = 0;  // sprite palette address of dot j in byte j of sc0|sc1
+    const bool spr_on = (g.flags & RF_SHOW_SPR) && nsl;
+    if (spr_on) {
+        for (uint32_t k = 0; k < nsl; k++) {
+            const uint32_t inf = sinfo[k];
+            const int o = xa - (int)(inf & 0xffu);
+            if (o <= -8 || o >= 8) continue;
+            const uint32_t rl = srow[k] & 0xffu, rh = (srow[k] >> 8) & 0xffu;
+            const uint32_t al = o >= 0 ? (rl << o) & 0xffu : rl >> (-o);
+            const uint32_t ah = o >= 0 ? (rh << o) & 0xffu : rh >> (-o);
+            const uint32_t nw = (al | ah) & ~filled;
+            if (!nw) continue;
+            filled |= nw;
+            if (inf & (1u << 13)) front_m |= nw;
+            const uint32_t cb = (inf >> 8) & 0x1fu;
+            for (int j = 0; j < 8; j++) {
+                if (nw & (0x80u >> j)) {
+                    uint32_t c = (((al >> (7 - j)) & 1u) | (((ah >> (7 - j)) & 1u) << 1)) | cb;
+                    if (j < 4) sc0 |= c << (8 * j); else sc1 |= c << (8 * (j - 4));
+                }
+            }
+        }
+    }
+    out[0] = 0; out[1] = 0;
+    for (int j = 0; j < 8; j++) {
+        const int xx = xa + j;
+        uint32_t pa = 0;
+        uint32_t b = ((wlo >> (7 - j)) & 1u) | (((whi >> (7 - j)) & 1u) << 1);
+        if (b) pa = b | ((((uint32_t)j < 8u - s) ? at0 : at1) << 2);
+        if ((g.flags & RF_HIDE_BG) && xx < 8) pa = 0;
+        if ((filled & (0x80u >> j)) && !((g.flags & RF_HIDE_SPR) && xx < 8)) {
+            if (!(pa & 3u) || (front_m & (0x80u >> j))) pa = ((j < 4 ? sc0 >> (8 * j) : sc1 >> (8 * (j - 4)))) & 0x1fu;
+        }
+        uint32_t px = rs.pal[pa];
+        uint32_t val = raw ? px : lut[px];
+        out[j >> 2] |= val << (8 * (j & 3));
+    }
+}
+
 }  // namespace fme

@@ -1,0 +1,273 @@
+// fme_fast.h - register-resident fast path of the 6502 interpreter.
+//
+// The full console (`Core`, fme_core.h) is the exact model; its I/O, PPU and NMI code is large and rarely
+// needed per instruction. Keeping the whole object in registers is not possible once that code is out of
+// line, so the loop works on `Hot`: the 6502 registers, the frame clock and the NMI threshold, held by value
+// (its address is never taken, so it stays in registers). Every instruction whose memory accesses are RAM or
+// PRG only runs here with the semantics of Core::execute_op (nes_core.hpp:645-1163); an instruction that
+// would touch $2000-$7FFF (PPU registers, joypads, OAM DMA), or code outside PRG, is handed to the exact
+// Core path with Hot written back first. Nothing here has side effects before that decision.
+#pragma once
+#include "fme_core.h"
+
+namespace fme {
+
+struct Hot {
+    uint32_t pc, a, x, y, sp, p;
+    int32_t exec_at, thresh;
+    uint32_t zero_skip, bad;
+};
+
+FME_HD void hot_out(const Hot& h, Core& c) {
+    c.pc = h.pc; c.a = h.a; c.x = h.x; c.y = h.y; c.sp = h.sp; c.p = h.p;
+    c.exec_at = h.exec_at; c.nmi_thresh = h.thresh; c.zero_skip = h.zero_skip != 0; c.bad_ops = h.bad;
+}
+FME_HD void hot_in(Hot& h, const Core& c) {
+    h.pc = c.pc; h.a = c.a; h.x = c.x; h.y = c.y; h.sp = c.sp; h.p = c.p;
+    h.exec_at = c.exec_at; h.thresh = c.nmi_thresh; h.zero_skip = c.zero_skip ? 1u : 0u; h.bad = c.bad_ops;
+}
+
+// Exact slow paths (the Core methods), out of line so the hot loop stays small.
+FME_NI void slow_presync(Core& c, int32_t J) {
+    c.cur = J;
+    c.sync_to(3 * (J + 1));
+}
+FME_NI int32_t slow_execute(Core& c, int32_t J, uint32_t opc) {
+    c.cur = J;
+    return opc <= 0xffu ? c.execute_op(opc) : c.execute_op(c.rd(c.pc));
+}
+
+struct Fast {
+    uint8_t* ram;            // lane base of the RAM slab
+    const uint8_t* prg;
+
+    FME_HD uint32_t P(uint32_t a) const { return FME_LDG(prg + (a & 0x7fffu)); }
+    FME_HD uint32_t pf(uint32_t a) const { a &= 0xffffu; return a >= 0x8000u ? P(a) : 0xffu; }
+    FME_HD uint32_t R(uint32_t a) const { return ram[il(a & 0x7ffu)]; }
+    FME_HD void W(uint32_t a, uint32_t v) const { ram[il(a & 0x7ffu)] = (uint8_t)v; }
+    // side-effect-free read of an address outside $2000-$7FFF
+    FME_HD uint32_t M(uint32_t a) const { return a >= 0x8000u ? P(a) : R(a); }
+    FME_HD static bool io(uint32_t a) { return a >= 0x2000u && a < 0x8000u; }
+
+    FME_HD static void zn(Hot& h, uint32_t v) {
+        v &= 0xffu;
+        h.p = (h.p & ~(F_Z | F_N)) | (v ? 0u : F_Z) | ((v & 0x80u) ? F_N : 0u);
+    }
+    FME_HD static void setf(Hot& h, uint32_t f, bool on) { h.p = on ? (h.p | f) : (h.p & ~f); }
+
+    // Execute the instruction with opcode `opc` at h.pc (pc in $8000-$FFFD). Returns the skip-cycle count, or
+    // -1 if the instruction needs the exact path (nothing was changed then).
+    FME_HD int32_t exec(Hot& h, uint32_t opc) const {
+        const uint32_t d = FME_DTAB(opc);
+        const uint32_t kind = d_kind(d), op = d_op(d);
+        const uint32_t b1 = P(h.pc + 1), b2 = P(h.pc + 2);
+        int32_t skip = 0;
+        uint32_t npc = (h.pc + 1) & 0xffffu;
+        switch (kind) {
+            case K_READ: case K_STORE: case K_RMW: {
+                const uint32_t mode = d_mode(d);
+                uint32_t loc = 0, base = 0;
+                switch (mode) {
+                    case M_IMM: loc = npc; npc += 1; break;
+                    case M_ZP: loc = b1; npc += 1; break;
+                    case M_ZPX: loc = (b1 + h.x) & 0xffu; npc += 1; break;
+                    case M_ZPY: loc = (b1 + h.y) & 0xffu; npc += 1; break;
+                    case M_ABS: loc = b1 | (b2 << 8); npc += 2; break;
+                    case M_ABSX: base = b1 | (b2 << 8); loc = (base + h.x) & 0xffffu; npc += 2; break;
+                    case M_ABSY: base = b1 | (b2 << 8); loc = (base + h.y) & 0xffffu; npc += 2; break;
+                    case M_INDX: { uint32_t za = (h.x + b1) & 0xffu; loc = R(za) | (R((za + 1) & 0xffu) << 8); npc += 1; break; }
+                    default: {  // M_INDY
+                        base = R(b1) | (R((b1 + 1) & 0xffu) << 8);
+                        loc = (base + h.y) & 0xffffu; npc += 1; break;
+                    }
+                }
+                if (io(loc)) return -1;
+                if (d_pen(d) && (mode == M_ABSX || mode == M_ABSY || mode == M_INDY) && ((base ^ loc) & 0xff00u)) skip += 1;
+                if (kind == K_READ) {
+                    const uint32_t m = M(loc);
+                    switch (op) {
+                        case R_ORA: h.a |= m; zn(h, h.a); break;
+                        case R_AND: h.a &= m; zn(h, h.a); break;
+                        case R_EOR: h.a ^= m; zn(h, h.a); break;
+                        case R_ADC: {
+                            uint32_t sum = h.a + m + ((h.p & F_C) ? 1u : 0u);
+                            setf(h, F_C, sum & 0x100u);
+                            setf(h, F_V, (h.a ^ sum) & (m ^ sum) & 0x80u);
+                            h.a = sum & 0xffu; zn(h, h.a);
+                            break;
+                        }
+                        case R_LDA: h.a = m; zn(h, h.a); break;
+                        case R_CMP: { uint32_t t = (h.a - m) & 0xffffu; setf(h, F_C, !(t & 0x100u)); zn(h, t); break; }
+                        case R_SBC: {
+                            uint32_t t = (h.a - m - ((h.p & F_C) ? 0u : 1u)) & 0xffffu;
+                            setf(h, F_C, !(t & 0x100u));
+                            setf(h, F_V, (h.a ^ t) & (~m ^ t) & 0x80u);
+                            h.a = t & 0xffu; zn(h, t);
+                            break;
+                        }
+                        case R_BIT: setf(h, F_Z, !(h.a & m)); setf(h, F_V, m & 0x40u); setf(h, F_N, m & 0x80u); break;
+                        case R_LDX: h.x = m; zn(h, h.x); break;
+                        case R_LDY: h.y = m; zn(h, h.y); break;
+                        case R_CPX: { uint32_t t = (h.x - m) & 0xffffu; setf(h, F_C, !(t & 0x100u)); zn(h, t); break; }
+                        default:    { uint32_t t = (h.y - m) & 0xffffu; setf(h, F_C, !(t & 0x100u)); zn(h, t); break; }
+                    }
+                } else if (kind == K_STORE) {
+                    if (loc < 0x2000u) W(loc, op == W_STA ? h.a : op == W_STX ? h.x : h.y);  // PRG writes are ignored
+                } else {
+                    uint32_t m = M(loc);
+                    const uint32_t c = (h.p & F_C) ? 1u : 0u;
+                    switch (op) {
+                        case X_ASL: setf(h, F_C, m & 0x80u); m = (m << 1) & 0xffu; break;
+                        case X_ROL: setf(h, F_C, m & 0x80u); m = ((m << 1) | c) & 0xffu; break;
+                        case X_LSR: setf(h, F_C, m & 1u); m >>= 1; break;
+                        case X_ROR: setf(h, F_C, m & 1u); m = (m >> 1) | (c << 7); break;
+                        case X_DEC: m = (m - 1) & 0xffu; break;
+                        default: m = (m + 1) & 0xffu; break;
+                    }
+                    zn(h, m);
+                    if (loc < 0x2000u) W(loc, m);
+                }
+                break;
+            }
+            case K_BRANCH: {
+                const uint32_t f = (h.p >> (op & 7u)) & 1u;
+                npc = (npc + 1) & 0xffffu;
+                if (f == ((op >> 3) & 1u)) {
+                    skip += 1;
+                    const uint32_t t = (uint32_t)((int32_t)npc + (int32_t)(int8_t)(uint8_t)b1) & 0xffffu;
+                    if ((t ^ npc) & 0xff00u) skip += 2;
+                    npc = t;
+                }
+                break;
+            }
+            case K_ACC: {
+                uint32_t m = h.a;
+                const uint32_t c = (h.p & F_C) ? 1u : 0u;
+                switch (op) {
+                    case X_ASL: setf(h, F_C, m & 0x80u); m = (m << 1) & 0xffu; break;
+                    case X_ROL: setf(h, F_C, m & 0x80u); m = ((m << 1) | c) & 0xffu; break;
+                    case X_LSR: setf(h, F_C, m & 1u); m >>= 1; break;
+                    default: setf(h, F_C, m & 1u); m = (m >> 1) | (c << 7); break;
+                }
+                zn(h, m);
+                h.a = m;
+                break;
+            }
+            case K_IMPL: {
+                switch (op) {
+                    case I_BRK: {
+                        uint32_t r = npc + 1;  // BRK skips its padding byte
+                        W(0x100u | h.sp, (r >> 8) & 0xffu); h.sp = (h.sp - 1) & 0xffu;
+                        W(0x100u | h.sp, r & 0xffu); h.sp = (h.sp - 1) & 0xffu;
+                        W(0x100u | h.sp, h.p | 0x30u); h.sp = (h.sp - 1) & 0xffu;
+                        h.p |= F_I;
+                        npc = P(0xfffe) | (P(0xffff) << 8);
+                        skip += 7;
+                        break;
+                    }
+                    case I_PHP: W(0x100u | h.sp, h.p); h.sp = (h.sp - 1) & 0xffu; break;
+                    case I_CLC: setf(h, F_C, false); break;
+                    case I_JSR: {
+                        uint32_t r = (npc + 1) & 0x1ffffu;
+                        W(0x100u | h.sp, (r >> 8) & 0xffu); h.sp = (h.sp - 1) & 0xffu;
+                        W(0x100u | h.sp, r & 0xffu); h.sp = (h.sp - 1) & 0xffu;
+                        npc = b1 | (b2 << 8);
+                        break;
+                    }
+                    case I_PLP: h.sp = (h.sp + 1) & 0xffu; h.p = R(0x100u | h.sp); break;
+                    case I_SEC: setf(h, F_C, true); break;
+                    case I_RTI: {
+                        h.sp = (h.sp + 1) & 0xffu; h.p = R(0x100u | h.sp);
+                        h.sp = (h.sp + 1) & 0xffu; uint32_t lo = R(0x100u | h.sp);
+                        h.sp = (h.sp + 1) & 0xffu; npc = lo | (R(0x100u | h.sp) << 8);
+                        break;
+                    }
+                    case I_PHA: W(0x100u | h.sp, h.a); h.sp = (h.sp - 1) & 0xffu; break;
+                    case I_JMP: npc = b1 | (b2 << 8); break;
+                    case I_CLI: setf(h, F_I, false); break;
+                    case I_RTS: {
+                        h.sp = (h.sp + 1) & 0xffu; uint32_t lo = R(0x100u | h.sp);
+                        h.sp = (h.sp + 1) & 0xffu; npc = ((lo | (R(0x100u | h.sp) << 8)) + 1) & 0xffffu;
+                        break;
+                    }
+                    case I_PLA: h.sp = (h.sp + 1) & 0xffu; h.a = R(0x100u | h.sp); zn(h, h.a); break;
+                    case I_JMPI: {
+                        const uint32_t loc = b1 | (b2 << 8);
+                        const uint32_t hiad = (loc & 0xff00u) | ((loc + 1) & 0xffu);
+                        if (io(loc) || io(hiad)) return -1;
+                        npc = M(loc) | (M(hiad) << 8);
+                        break;
+                    }
+                    case I_SEI: setf(h, F_I, true); break;
+                    case I_DEY: h.y = (h.y - 1) & 0xffu; zn(h, h.y); break;
+                    case I_TXA: h.a = h.x; zn(h, h.a); break;
+                    case I_TYA: h.a = h.y; zn(h, h.a); break;
+                    case I_TXS: h.sp = h.x; break;
+                    case I_TAY: h.y = h.a; zn(h, h.y); break;
+                    case I_TAX: h.x = h.a; zn(h, h.x); break;
+                    case I_CLV: setf(h, F_V, false); break;
+                    case I_TSX: h.x = h.sp; zn(h, h.x); break;
+                    case I_INY: h.y = (h.y + 1) & 0xffu; zn(h, h.y); break;
+                    case I_DEX: h.x = (h.x - 1) & 0xffu; zn(h, h.x); break;
+                    case I_CLD: setf(h, F_D, false); break;
+                    case I_INX: h.x = (h.x + 1) & 0xffu; zn(h, h.x); break;
+                    case I_NOP: break;
+                    default: setf(h, F_D, true); break;  // SED
+                }
+                break;
+            }
+            case K_BAD_ZP: h.bad++; npc += 1; break;
+            case K_BAD_ABS: h.bad++; npc += 2; break;
+            case K_BAD_ABSX: {
+                const uint32_t b = b1 | (b2 << 8);
+                if (((b + h.x) ^ b) & 0xff00u) skip += 1;
+                h.bad++; npc += 2;
+                break;
+            }
+            default: h.bad++; break;
+        }
+        h.pc = npc & 0xffffu;
+        if (kind >= K_IMPL) skip += (int32_t)d_cycles(d);
+        return skip;
+    }
+};
+
+// One scheduling unit of the frame loop (the body of nes_core.hpp:1169-1201) on the register state.
+// Returns false when exec_at reached the frame end (the caller then runs Core::end_frame via hot_out).
+FME_HD bool hot_step(Hot& h, Core& c, const Fast& f) {
+    if (h.exec_at >= FRAME_ITERS) return false;
+    const int32_t J = h.exec_at;
+    if (3 * (J + 1) >= h.thresh) {
+        hot_out(h, c);
+        slow_presync(c, J);
+        hot_in(h, c);
+        if (h.exec_at != J) return true;  // an NMI was taken before this instruction
+    }
+    // idle-loop test with rd_prg_fast semantics (0xff outside PRG, nes_core.hpp:153, 1178)
+    const uint32_t op0 = h.pc >= 0x8000u ? f.P(h.pc) : 0xffu;
+    if (op0 == 0x4Cu && (f.pf(h.pc + 1) | (f.pf(h.pc + 2) << 8)) == h.pc) {
+        int32_t lim_end = FRAME_ITERS - J;
+        int32_t lim_nmi = h.thresh - 3 * (J + 1);
+        int32_t k1 = lim_end > 0 ? (lim_end + 2) / 3 : 0;
+        int32_t k2 = lim_nmi > 0 ? (lim_nmi + 8) / 9 : 0;
+        int32_t k = k1 < k2 ? k1 : k2;
+        if (k > 1) {
+            h.exec_at = J + 3 * (k - 1);
+            h.zero_skip = 0;
+            return true;
+        }
+    }
+    const bool in_prg = h.pc >= 0x8000u && h.pc <= 0xfffdu;  // operand bytes then come from PRG too
+    const uint32_t opc = in_prg ? op0 : 0x100u;
+    int32_t S = in_prg ? f.exec(h, opc) : -1;
+    if (S < 0) {
+        hot_out(h, c);
+        S = slow_execute(c, J, opc);
+        hot_in(h, c);
+    }
+    h.exec_at = J + (S >= 1 ? S : 1);
+    h.zero_skip = S <= 0 ? 1u : 0u;
+    return true;
+}
+
+}  // namespace fme

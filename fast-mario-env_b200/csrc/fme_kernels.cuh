@@ -14,6 +14,7 @@ extern uint32_t g_host_dtab[256];
 #endif
 #include "fme_core.h"
 #include "fme_agent.h"
+#include "fme_fast.h"
 #include "fme_render.h"
 
 namespace fme {
@@ -76,9 +77,9 @@ __device__ __forceinline__ void bind_core(Core& c, const Dev& d, uint8_t* sm, in
 // at the warp's minimum PC run it, so lanes that took a shorter path wait at the join point and the warp
 // re-converges on identical instructions (results cannot depend on the schedule: lanes are independent).
 // Lanes at a frame boundary always proceed. Returns true if this lane may step now.
-__device__ __forceinline__ bool minpc_turn(bool running, const Core& c) {
-    const bool exec = running && c.exec_at < FRAME_ITERS;
-    const uint32_t key = exec ? c.pc : 0xffffffffu;
+__device__ __forceinline__ bool minpc_turn(bool running, const Hot& h) {
+    const bool exec = running && h.exec_at < FRAME_ITERS;
+    const uint32_t key = exec ? h.pc : 0xffffffffu;
     const uint32_t mn = __reduce_min_sync(FULL, key);
     return running && (!exec || key == mn);
 }

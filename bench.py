@@ -187,9 +187,10 @@ def main():
         import torch.distributed as dist
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
 
+    from fast_mario_env_b200 import shard
     rom = build_rom(0)
     E = args.envs
-    off = rank * E
+    off = shard.env_offset(rank, E)
     env = fme.CudaVecEnv(level_names(E), E, seed=0, sticky=0.25, noop_max=30, max_steps=2000, skip=4, frame_stack=4,
                          maxpool=True, device=dev, rom=rom, env_offset=off)
     total = args.warmup + args.steps
@@ -215,12 +216,10 @@ def main():
     clk = clocks.stop()
     ms = ev0.elapsed_time(ev1)
     env.check()
-    ms_t = torch.tensor([ms], device=dev, dtype=torch.float64)
     if dist:
         dist.barrier()
-        dist.all_reduce(ms_t, op=dist.ReduceOp.MAX)
-    ms_max = float(ms_t.item())
-    value = world * E * args.steps / (ms_max / 1000.0)
+    ms_max = shard.max_over_ranks(ms, device=dev)
+    value = shard.job_throughput(world, E, args.steps, ms_max)
     ms_step = ms_max / args.steps
     kernel_ms = ms / args.steps  # one k_step launch per step on this rank
 
@@ -240,12 +239,10 @@ def main():
             fenv.step(hacts[t])
         dt = time.perf_counter() - t0
         fenv.check()
-        dt_t = torch.tensor([dt], device=dev, dtype=torch.float64)
-        if dist:
-            dist.all_reduce(dt_t, op=dist.ReduceOp.MAX)
+        dt_max = shard.max_over_ranks(dt, device=dev)
         h2d = E * 8
         d2h = E * (4 * 84 * 84 + 4 + 1 + 1 + 40 + 8 + 4)  # + final_obs rows of the envs that ended
-        e2e = {"value": world * E * args.steps / float(dt_t.item()), "unit": UNIT, "h2d_bytes_per_step": h2d * world,
+        e2e = {"value": shard.job_throughput(world, E, args.steps, dt_max * 1000.0), "unit": UNIT, "h2d_bytes_per_step": h2d * world,
                "d2h_bytes_per_step": d2h * world, "api": "FastVecEnv.step (numpy in/out, full stacks, infos)"}
         fenv.close()
 

@@ -405,6 +405,13 @@ __global__ void __launch_bounds__(32) k_raw(RawParams P) {
     }
 }
 
+// PPU log slots for fme_raw_frame_static, reserved with the module rather than by cudaMalloc. Callers that
+// drive a few consoles next to a process owning the rest of the device's memory (a trainer whose caching
+// allocator has reserved HBM, where a cudaMalloc can fail or synchronise the device) step frames through it
+// without any allocation. Slot layout as d.logs: two slots per console, k_raw writes slot 0.
+constexpr size_t STATIC_SLOT_BYTES = (size_t)SLOT_HDR_BYTES + (size_t)FME_STATIC_LOG_CAPACITY * 16u;
+static __device__ __align__(256) uint8_t g_raw_scratch[(size_t)FME_STATIC_MAX_CONSOLES * 2 * STATIC_SLOT_BYTES];
+
 // Power-on state (Emulator(rom) + Reset, nes_core.hpp:128-147) for raw consoles.
 __global__ void __launch_bounds__(32) k_power(Dev d) {
     extern __shared__ __align__(16) uint8_t sm[];
@@ -460,6 +467,22 @@ int fail(int code, const std::string& msg) { g_err = msg; return code; }
 
 std::mutex g_const_mu;
 bool g_const_done[64];
+
+std::mutex g_scratch_mu;
+void* g_scratch_addr[64];
+
+// Device address of g_raw_scratch on `device`, which must be current: looked up once per device.
+int static_scratch(int device, uint8_t** out) {
+    std::lock_guard<std::mutex> lk(g_scratch_mu);
+    if (device < 0 || device >= 64) return fail(FME_E_ARG, "device ordinal out of range");
+    if (!g_scratch_addr[device]) {
+        void* p = nullptr;
+        CK(cudaGetSymbolAddress(&p, g_raw_scratch));
+        g_scratch_addr[device] = p;
+    }
+    *out = static_cast<uint8_t*>(g_scratch_addr[device]);
+    return FME_OK;
+}
 
 int ensure_constants(int device) {
     std::lock_guard<std::mutex> lk(g_const_mu);
@@ -960,6 +983,26 @@ void fme_raw_destroy(FmeRaw* r) {
     cudaFree(r->d_prg); cudaFree(r->d_chr); cudaFree(r->d_lut); cudaFree(r->d_err); cudaFree(r->d_screens);
     cudaFree(r->d_bk_slab); cudaFree(r->d_bk_vram); cudaFree(r->d_bk_scal);
     delete r;
+}
+
+int fme_raw_frame_static(FmeRaw* r, const uint8_t* d_buttons, uint8_t* d_screens, int32_t render, void* stream) {
+    if (!r || !d_buttons) return fail(FME_E_ARG, "null raw / buttons");
+    if (render && !d_screens) return fail(FME_E_ARG, "render needs a screen buffer");
+    if (r->n > FME_STATIC_MAX_CONSOLES)
+        return fail(FME_E_ARG, "fme_raw_frame_static takes at most " + std::to_string(FME_STATIC_MAX_CONSOLES) +
+                                   " consoles, the handle has " + std::to_string(r->n));
+    CK(cudaSetDevice(r->device));
+    uint8_t* scratch = nullptr;
+    int rc = static_scratch(r->device, &scratch);
+    if (rc) return rc;
+    RawParams P;
+    P.d = make_dev(r->st, r->d_prg, r->d_chr, r->nt, r->d_lut, r->d_err);
+    P.d.logs = scratch;
+    P.d.log_cap = FME_STATIC_LOG_CAPACITY;
+    P.buttons = d_buttons; P.render = render ? 1 : 0; P.screens = d_screens;
+    k_raw<<<(r->n + 31) / 32, 32, SLAB_BYTES, (cudaStream_t)stream>>>(P);
+    CK(cudaGetLastError());
+    return FME_OK;
 }
 
 int fme_resize(const uint8_t* d_src, uint8_t* d_dst, int32_t n, void* stream) {

@@ -133,6 +133,21 @@ int fme_raw_bad_ops(FmeRaw* raw, int64_t* out);
 int fme_raw_poll_error(FmeRaw* raw, uint32_t* status);
 void fme_raw_destroy(FmeRaw* raw);
 
+/* One NES frame like fme_raw_frame, allocating nothing. No counterpart in the reference.
+ * The per-frame PPU log (the scratch fme_raw_frame keeps in the handle) lives in a fixed device array
+ * compiled into the library: FME_STATIC_MAX_CONSOLES consoles at FME_STATIC_LOG_CAPACITY records a frame
+ * (about 4.3 MB). Handles with more consoles are rejected with FME_E_ARG; a frame with more records sets
+ * FME_ST_LOG_OVERFLOW. render != 0 writes the 240x256 palette-value screens into d_screens ((n, 240, 256)
+ * uint8, caller-owned; may be NULL when render == 0). Nothing in the array has to start at zero: every
+ * frame rewrites its slot header before the records it reads back. The first call on a device looks the
+ * array's address up (cudaGetSymbolAddress) with that device current; make it before any stream capture.
+ * All calls on one device share the array, so calls that can overlap (other streams, other threads)
+ * race and must be ordered by the caller. Async. */
+#define FME_STATIC_MAX_CONSOLES 64
+#define FME_STATIC_LOG_CAPACITY 2048
+int fme_raw_frame_static(FmeRaw* raw, const uint8_t* d_buttons, uint8_t* d_screens, int32_t render,
+                         void* stream);
+
 /* ---- helpers ---- */
 /* nes-py master palette, 64 x 0xRRGGBB (replaces fm_palette, csrc/fastmario.cpp:637). */
 void fme_palette(uint32_t* out64);

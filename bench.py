@@ -67,10 +67,13 @@ def read_peaks():
 
 
 def committed_traffic():
-    p = os.path.join(ROOT, "profiles", "k_step_traffic.json")
+    """DRAM bytes per env-step of k_step from the committed ncu summary (read + write, small-case capture
+    scaled by env count: the per-env state, stack and log traffic grow in proportion to the envs)."""
+    p = os.path.join(ROOT, "profiles", "k_step_full_config1_4096.md")
     if os.path.exists(p):
-        d = json.load(open(p))
-        return d.get("dram_bytes_per_env_step")
+        for line in open(p):
+            if line.startswith("traffic_per_env_step_bytes"):
+                return float(line.split("=")[1])
     return None
 
 

@@ -226,7 +226,8 @@ def main():
     ms_step = ms_max / args.steps
     kernel_ms = ms / args.steps  # one k_step launch per step on this rank
 
-    # ---- end to end through the FastVecEnv host API (host actions in, host outputs out, every step)
+    # ---- end to end through the C ABI with host buffers (FastVecEnv.step_arrays = fme_step between a
+    # pinned-host action upload and pinned-host copies of every output; final_obs rows of ended envs)
     e2e = None
     if not args.no_e2e:
         fenv = fme.FastVecEnv(level_names(E), E, seed=0, sticky=0.25, noop_max=30, max_steps=2000, maxpool=True,
@@ -234,19 +235,22 @@ def main():
         fenv.reset()
         hacts = np.random.default_rng(99 + rank).integers(0, 7, (total, E))
         for t in range(args.warmup):
-            fenv.step(hacts[t])
+            fenv.step_arrays(hacts[t])
         if dist:
             dist.barrier()
+        n_final = 0
         t0 = time.perf_counter()
         for t in range(args.warmup, total):
-            fenv.step(hacts[t])
+            n_final += len(fenv.step_arrays(hacts[t])[5])
         dt = time.perf_counter() - t0
         fenv.check()
         dt_max = shard.max_over_ranks(dt, device=dev)
         h2d = E * 8
-        d2h = E * (4 * 84 * 84 + 4 + 1 + 1 + 40 + 8 + 4)  # + final_obs rows of the envs that ended
-        e2e = {"value": shard.job_throughput(world, E, args.steps, dt_max * 1000.0), "unit": UNIT, "h2d_bytes_per_step": h2d * world,
-               "d2h_bytes_per_step": d2h * world, "api": "FastVecEnv.step (numpy in/out, full stacks, infos)"}
+        d2h = E * (4 * 84 * 84 + 4 + 1 + 1 + 4 * 10 + 8 + 4) + (n_final * 4 * 84 * 84) // args.steps
+        e2e = {"value": shard.job_throughput(world, E, args.steps, dt_max * 1000.0), "unit": UNIT,
+               "h2d_bytes_per_step": h2d * world, "d2h_bytes_per_step": d2h * world,
+               "api": "FastVecEnv.step_arrays: fme_step with pinned host actions in and every output "
+                      "(stacked obs, rew, term, trunc, info, episode stats, final_obs rows) copied to host"}
         fenv.close()
 
     peak, peak_kind = read_peaks()

@@ -59,9 +59,9 @@ __global__ void __launch_bounds__(32) k_boot(BootParams P) {
     // Boot protocol of SuperMarioBrosEnv (fastmario.cpp:422-445), one frame per call of the state machine:
     // phase 0 fa(8), 1 fa(0), then loop A {2: fa(8); write level; 3: fa(0); $7A0=0} while time==0,
     // then loop B {4: fa(8), 5: fa(0)} while time >= tl.
-    Hot h;
-    hot_in(h, c);
     const Fast fst{c.ram, d.prg};
+    Hot h;
+    hot_in(h, c, fst);
     while (__any_sync(FULL, running)) {
         if (minpc_turn(running, h)) {
             if (!hot_step(h, c, fst)) {
@@ -88,7 +88,7 @@ __global__ void __launch_bounds__(32) k_boot(BootParams P) {
                 if (next >= 0 && frames >= P.boot_cap) { c.status |= ST_BOOT_CAP; next = -1; }
                 if (next < 0) running = false;
                 else { phase = next; begin_frame(c, slot, btn, d.log_cap); }
-                hot_in(h, c);
+                hot_in(h, c, fst);
             }
         }
     }
@@ -162,15 +162,15 @@ __global__ void __launch_bounds__(32) k_step(StepParams P) {
     bool running = active;
     if (active) ag.start(c, ev, cfg, act, d.logs + slot_off(e, 0, cap), d.logs + slot_off(e, 1, cap));
     // one emulated instruction per lane per iteration; the vote keeps the warp converged at the loop head
-    Hot h;
-    hot_in(h, c);
     const Fast fst{c.ram, d.prg};
+    Hot h;
+    hot_in(h, c, fst);
     while (__any_sync(FULL, running)) {
         if (minpc_turn(running, h) && !hot_step(h, c, fst)) {
             hot_out(h, c);
             c.end_frame();
             running = ag.on_frame_end(c, ev, cfg);
-            hot_in(h, c);
+            hot_in(h, c, fst);
         }
     }
     hot_out(h, c);
@@ -371,16 +371,16 @@ __global__ void __launch_bounds__(32) k_raw(RawParams P) {
     uint8_t* slot = d.logs + slot_off(e, 0, d.log_cap);
     bool running = active;
     if (active) begin_frame(c, slot, P.buttons[e], d.log_cap);
-    Hot h;
-    hot_in(h, c);
     const Fast fst{c.ram, d.prg};
+    Hot h;
+    hot_in(h, c, fst);
     while (__any_sync(FULL, running)) {
         if (minpc_turn(running, h) && !hot_step(h, c, fst)) {
             hot_out(h, c);
             c.end_frame();
             close_frame(c, slot);
             running = false;
-            hot_in(h, c);
+            hot_in(h, c, fst);
         }
     }
     hot_out(h, c);

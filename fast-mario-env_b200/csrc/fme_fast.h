@@ -16,16 +16,8 @@ struct Hot {
     uint32_t pc, a, x, y, sp, p;
     int32_t exec_at, thresh;
     uint32_t zero_skip, bad;
+    uint32_t op, b1, b2;  // bytes at pc, pc+1, pc+2 as rd_prg_fast reads them (0xff outside PRG)
 };
-
-FME_HD void hot_out(const Hot& h, Core& c) {
-    c.pc = h.pc; c.a = h.a; c.x = h.x; c.y = h.y; c.sp = h.sp; c.p = h.p;
-    c.exec_at = h.exec_at; c.nmi_thresh = h.thresh; c.zero_skip = h.zero_skip != 0; c.bad_ops = h.bad;
-}
-FME_HD void hot_in(Hot& h, const Core& c) {
-    h.pc = c.pc; h.a = c.a; h.x = c.x; h.y = c.y; h.sp = c.sp; h.p = c.p;
-    h.exec_at = c.exec_at; h.thresh = c.nmi_thresh; h.zero_skip = c.zero_skip ? 1u : 0u; h.bad = c.bad_ops;
-}
 
 // Exact slow paths (the Core methods), out of line so the hot loop stays small.
 FME_NI void slow_presync(Core& c, int32_t J) {
@@ -60,7 +52,7 @@ struct Fast {
     FME_HD int32_t exec(Hot& h, uint32_t opc) const {
         const uint32_t d = FME_DTAB(opc);
         const uint32_t kind = d_kind(d), op = d_op(d);
-        const uint32_t b1 = P(h.pc + 1), b2 = P(h.pc + 2);
+        const uint32_t b1 = h.b1, b2 = h.b2;  // pc <= $FFFD: both come from PRG
         int32_t skip = 0;
         uint32_t npc = (h.pc + 1) & 0xffffu;
         switch (kind) {
@@ -232,6 +224,24 @@ struct Fast {
     }
 };
 
+// Prefetch of the instruction bytes at the new pc: the next iteration's idle test, decode and the
+// scheduler's vote all read them, so the loads overlap the loop head instead of following it.
+FME_HD void fetch(Hot& h, const Fast& f) {
+    h.op = h.pc >= 0x8000u ? f.P(h.pc) : 0xffu;
+    h.b1 = f.pf(h.pc + 1);
+    h.b2 = f.pf(h.pc + 2);
+}
+FME_HD bool idle_loop(const Hot& h) { return h.op == 0x4Cu && (h.b1 | (h.b2 << 8)) == h.pc; }  // JMP to itself
+FME_HD void hot_out(const Hot& h, Core& c) {
+    c.pc = h.pc; c.a = h.a; c.x = h.x; c.y = h.y; c.sp = h.sp; c.p = h.p;
+    c.exec_at = h.exec_at; c.nmi_thresh = h.thresh; c.zero_skip = h.zero_skip != 0; c.bad_ops = h.bad;
+}
+FME_HD void hot_in(Hot& h, const Core& c, const Fast& f) {
+    h.pc = c.pc; h.a = c.a; h.x = c.x; h.y = c.y; h.sp = c.sp; h.p = c.p;
+    h.exec_at = c.exec_at; h.thresh = c.nmi_thresh; h.zero_skip = c.zero_skip ? 1u : 0u; h.bad = c.bad_ops;
+    fetch(h, f);
+}
+
 // One scheduling unit of the frame loop (the body of nes_core.hpp:1169-1201) on the register state.
 // Returns false when exec_at reached the frame end (the caller then runs Core::end_frame via hot_out).
 FME_HD bool hot_step(Hot& h, Core& c, const Fast& f) {
@@ -240,12 +250,11 @@ FME_HD bool hot_step(Hot& h, Core& c, const Fast& f) {
     if (3 * (J + 1) >= h.thresh) {
         hot_out(h, c);
         slow_presync(c, J);
-        hot_in(h, c);
+        hot_in(h, c, f);
         if (h.exec_at != J) return true;  // an NMI was taken before this instruction
     }
     // idle-loop test with rd_prg_fast semantics (0xff outside PRG, nes_core.hpp:153, 1178)
-    const uint32_t op0 = h.pc >= 0x8000u ? f.P(h.pc) : 0xffu;
-    if (op0 == 0x4Cu && (f.pf(h.pc + 1) | (f.pf(h.pc + 2) << 8)) == h.pc) {
+    if (idle_loop(h)) {
         int32_t lim_end = FRAME_ITERS - J;
         int32_t lim_nmi = h.thresh - 3 * (J + 1);
         int32_t k1 = lim_end > 0 ? (lim_end + 2) / 3 : 0;
@@ -258,12 +267,14 @@ FME_HD bool hot_step(Hot& h, Core& c, const Fast& f) {
         }
     }
     const bool in_prg = h.pc >= 0x8000u && h.pc <= 0xfffdu;  // operand bytes then come from PRG too
-    const uint32_t opc = in_prg ? op0 : 0x100u;
+    const uint32_t opc = in_prg ? h.op : 0x100u;
     int32_t S = in_prg ? f.exec(h, opc) : -1;
     if (S < 0) {
         hot_out(h, c);
         S = slow_execute(c, J, opc);
-        hot_in(h, c);
+        hot_in(h, c, f);
+    } else {
+        fetch(h, f);
     }
     h.exec_at = J + (S >= 1 ? S : 1);
     h.zero_skip = S <= 0 ? 1u : 0u;

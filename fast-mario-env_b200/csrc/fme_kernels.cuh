@@ -76,12 +76,14 @@ __device__ __forceinline__ void bind_core(Core& c, const Dev& d, uint8_t* sm, in
 // Warp scheduling of the emulation loop: among the lanes that are about to execute an instruction only those
 // at the warp's minimum PC run it, so lanes that took a shorter path wait at the join point and the warp
 // re-converges on identical instructions (results cannot depend on the schedule: lanes are independent).
-// Lanes at a frame boundary always proceed. Returns true if this lane may step now.
+// Lanes spinning in a `JMP *` idle loop wait until every other lane is idle or at the frame boundary, and
+// lanes at the frame boundary wait for all others: the warp then takes the idle fast-forward, the PPU catch-up
+// before the NMI and the frame end together instead of one lane at a time. Returns true if this lane may step.
 __device__ __forceinline__ bool minpc_turn(bool running, const Hot& h) {
-    const bool exec = running && h.exec_at < FRAME_ITERS;
-    const uint32_t key = exec ? h.pc : 0xffffffffu;
+    uint32_t key = 0xffffffffu;
+    if (running) key = h.exec_at >= FRAME_ITERS ? 0x20000u : (idle_loop(h) ? 0x10000u : 0u) | h.pc;
     const uint32_t mn = __reduce_min_sync(FULL, key);
-    return running && (!exec || key == mn);
+    return running && key == mn;
 }
 
 // coalesced copy of a whole slab between HBM and shared memory (warp-wide)

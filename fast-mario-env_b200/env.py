@@ -317,6 +317,25 @@ class FastVecEnv:
         self.step_async(actions)
         return self.step_wait()
 
+    def step_arrays(self, actions):
+        """One step with host buffers and no per-env Python objects, at the level of the reference's
+        fm_step_async + fm_step_wait (fastmario.cpp:599-617): actions in, then (obs, rew, term, trunc, info,
+        final_obs) where obs/rew/info are views of the pinned host buffers (valid until the next step),
+        info is (N, len(INFO_FIELDS)) int32 and final_obs maps env index -> its final stacked frame
+        for the envs whose episode ended."""
+        self.step_async(actions)
+        self._event.synchronize()
+        self._pending = False
+        term = self._term.numpy()
+        trunc = self._trunc.numpy()
+        ended = np.flatnonzero(term | trunc)
+        fin = {}
+        if len(ended):
+            idx = _torch().from_numpy(ended).to(self.env.dev)
+            rows = self.env.final_obs.index_select(0, idx).cpu().numpy()
+            fin = {int(i): rows[k] for k, i in enumerate(ended)}
+        return self._obs.numpy(), self._rew.numpy(), term, trunc, self._info.numpy(), fin
+
     def ram(self, i: int) -> np.ndarray:
         out = np.zeros(0x800, np.uint8)
         _torch().cuda.synchronize(self.env.dev)

@@ -73,6 +73,29 @@ def test_fastvecenv_matches_cudavecenv(rom):
             assert infos[i]["x_pos"] == int(i2["x_pos"][i])
 
 
+def test_step_arrays_matches_step(rom):
+    kw = dict(seed=5, sticky=0.25, noop_max=30, maxpool=True, max_steps=40, rom=rom)
+    f = fme.FastVecEnv("1-1", 8, **kw)
+    g = fme.FastVecEnv("1-1", 8, **kw)
+    f.reset(); g.reset()
+    rng = np.random.default_rng(6)
+    ended = 0
+    for _ in range(60):
+        a = rng.integers(0, 7, 8)
+        o1, r1, te1, tr1, infos = f.step(a)
+        o2, r2, te2, tr2, inf2, fin = g.step_arrays(a)
+        assert np.array_equal(o1, o2) and np.array_equal(r1, r2)
+        assert np.array_equal(te1, te2) and np.array_equal(tr1, tr2)
+        for i in range(8):
+            assert infos[i]["x_pos"] == inf2[i, 0] and infos[i]["score"] == inf2[i, 3]
+            if te1[i] or tr1[i]:
+                assert np.array_equal(infos[i]["final_obs"], fin[i])
+                ended += 1
+        assert set(fin) == {i for i in range(8) if te1[i] or tr1[i]}
+    assert ended > 0
+    f.close(); g.close()
+
+
 def test_resize_matches_cv2_golden():
     g = np.load(os.path.join(GOLD, "resize.npz"))
     out = fme.resize_area(g["src"])

@@ -68,8 +68,9 @@ struct Core {
     // ---- frame log
     uint4* rec;     // record area of the current slot
     int32_t nrec, cap;
-    bool seg_open;        // the last segment may still be extended by later dots of the same line
+    bool seg_open;        // the last segment may still be extended by later dots
     uint32_t seg_w0;
+    uint32_t seg_y1;      // its last line
     int32_t seg_idx;      // record index of that segment
     uint32_t seg_reads;   // TOUCH_* inputs its pixels depend on
     int32_t vram_burst;   // VRAM write records since the last segment that reads VRAM
@@ -184,10 +185,20 @@ struct Core {
         return TOUCH_ALL | (show_bg ? (TOUCH_BG | TOUCH_VRAM) : 0u) | (show_spr ? (TOUCH_SPR | TOUCH_VRAM) : 0u);
     }
     FME_HD void log_seg(uint32_t x0, uint32_t x1) {
-        if (seg_open && ((seg_w0 >> 4) & 0xffu) == scanline && (seg_w0 >> 21) == x0) {
-            seg_w0 = (seg_w0 & ~(0x1ffu << 21)) | (x1 << 21);
-            rec[seg_idx].x = seg_w0;
-            return;
+        if (seg_open) {
+            const uint32_t end = seg_w0 >> 21;
+            if (seg_y1 == scanline && end == x0) {                    // continues on the same line
+                seg_w0 = (seg_w0 & ~(0x1ffu << 21)) | (x1 << 21);
+                rec[seg_idx].x = seg_w0;
+                return;
+            }
+            if (seg_y1 + 1 == scanline && end == 256u && x0 == 0) {  // continues on the next line
+                seg_w0 = (seg_w0 & ~(0x1ffu << 21)) | (x1 << 21);
+                seg_y1 = scanline;
+                rec[seg_idx].x = seg_w0;
+                rec[seg_idx].w = seg_y1;
+                return;
+            }
         }
         const uint32_t rd_ = reads_now();
         if (rd_ & TOUCH_VRAM) {
@@ -196,11 +207,11 @@ struct Core {
         }
         uint32_t w0 = REC_SEG | (scanline << 4) | (x0 << 12) | (x1 << 21);
         uint32_t w1 = v | (fine_x << 16) | (render_flags() << 19);
-        uint32_t w2 = (ev_pend ? 1u : 0u) | (ev_y << 1) | (oam_addr << 9);
+        uint32_t w2 = (ev_pend ? 1u : 0u) | (ev_y << 1) | (oam_addr << 9) | ((t & 0x1fu) << 17) | (((t >> 10) & 1u) << 22);
         const bool room = nrec < cap;
-        emit(w0, w1, w2);
+        emit(w0, w1, w2, scanline);
         seg_open = room;
-        seg_w0 = w0; seg_idx = nrec - 1; seg_reads = rd_;
+        seg_w0 = w0; seg_y1 = scanline; seg_idx = nrec - 1; seg_reads = rd_;
     }
 
     // ================================================================ sprite evaluation (nes_core.hpp:336-349)
@@ -290,7 +301,11 @@ struct Core {
         return st;
     }
     FME_HD void ppu_addr(uint32_t val) {
-        if (first_write) { t = (t & 0x00ffu) | ((val & 0x3fu) << 8); first_write = 0; }
+        if (first_write) {
+            const uint32_t nt_ = (t & 0x00ffu) | ((val & 0x3fu) << 8);
+            if ((nt_ ^ t) & 0x0400u) touch(TOUCH_BG);  // t's x bits reach v at the next dot-258 copy
+            t = nt_; first_write = 0;
+        }
         else { t = (t & 0xff00u) | val; v = t; first_write = 1; touch(TOUCH_BG); }
     }
     FME_HD uint32_t ppu_get_data() {
@@ -422,11 +437,46 @@ struct Core {
         zero_skip = false;
     }
 
+    // How many of the next `avail` whole visible lines (from dot 1 of the current line) can be advanced in
+    // closed form: all of them unless a line could test sprite-0 pixels, which must then run dot by dot.
+    FME_HD int bulk_lines(int avail) const {
+        int L = avail < 240 - (int)scanline ? avail : 240 - (int)scanline;
+        if (L <= 0 || !show_bg || !show_spr || s0hit) return L;
+        if (s0_in_list()) return 0;                    // this line's list (as evaluated so far) holds sprite 0
+        if (oam_addr >= 4) return L;                   // later lists start past sprite 0
+        const int range = long_spr ? 16 : 8;
+        const int c0 = (int)OAM(0) + 1, c1 = (int)OAM(0) + range;   // lines whose list (line-1) holds sprite 0
+        const int y_lo = (int)scanline + 1 > c0 ? (int)scanline + 1 : c0;
+        const int y_hi = (int)scanline + L - 1 < c1 ? (int)scanline + L - 1 : c1;
+        if (y_lo <= y_hi) L = y_lo - (int)scanline;
+        return L;
+    }
+    // L >= 1 whole visible lines without sprite-0 tests: one segment (extended), the scroll increments of
+    // dots 1-256, the dot-257 fine-y increment and the dot-258 copy, the lazy evaluation of the last line.
+    FME_HD void run_lines(int L) {
+        log_seg(0, 256);
+        if (L > 1 && seg_open) { seg_y1 = scanline + (uint32_t)L - 1u; rec[seg_idx].w = seg_y1; }
+        if (L > 1 && !seg_open) status |= ST_LOG_OVERFLOW;  // the per-line records would not have fit either
+        if (show_bg) {
+            if (show_spr) v = (v & ~0x041fu & 0xffffu) | (t & 0x041fu);
+            else if (L & 1) v ^= 0x0400u;                 // 32 coarse-x increments per line
+            v = fine_y_add(v, L);
+        }
+        ev_pend = true; ev_y = scanline + (uint32_t)L - 1u;
+        scanline += (uint32_t)L;
+        ppu_calls += 341 * L;
+        if (scanline >= 240) pstate = PS_POST;
+    }
+
     // advance the PPU by n PPU::cycle calls (semantics of nes_core.hpp:534-616)
     FME_NI void ppu_run(int32_t n) {
         while (n > 0) {
             int c = (int)pcyc;
             if (pstate == PS_RENDER) {
+                if (c == 1 && n >= 341) {
+                    const int L = bulk_lines(n / 341);
+                    if (L > 0) { run_lines(L); n -= 341 * L; continue; }
+                }
                 if (c >= 1 && c <= 256) {
                     int k = n < 257 - c ? n : 257 - c;
                     dots(c - 1, c - 1 + k);
@@ -442,7 +492,6 @@ struct Core {
                     pcyc += (uint32_t)k; ppu_calls += k; n -= k;
                 } else if (c >= 341) {
                     ev_pend = true; ev_y = scanline;   // end-of-line sprite evaluation (lazy)
-                    seg_open = false;
                     ++scanline;
                     pcyc = 1; ppu_calls++; n--;
                     if (scanline >= 240) pstate = PS_POST;
@@ -470,6 +519,15 @@ struct Core {
                     int k = n < 341 - c ? n : 341 - c;
                     pcyc += (uint32_t)k; ppu_calls += k; n -= k;
                 }
+            } else if (!(c == 1 && scanline == 241) && c >= 1 && c <= 341 && scanline >= 241 && scanline <= 260) {
+                // vertical blank after the flag dot: nothing happens until the pre-render line, so advance
+                // by position (each line is dots 1..340 and its line end, 341 calls)
+                const int end = 20 * 341;
+                int pos = ((int)scanline - 241) * 341 + (c - 1);
+                const int k = n < end - pos ? n : end - pos;
+                pos += k; ppu_calls += k; n -= k;
+                if (pos >= end) { pstate = PS_PRE; scanline = 0; pcyc = 1; even = even ? 0u : 1u; }
+                else { scanline = 241u + (uint32_t)(pos / 341); pcyc = (uint32_t)(pos % 341) + 1u; }
             } else {  // vertical blank
                 if (c >= 341) {
                     ++scanline;

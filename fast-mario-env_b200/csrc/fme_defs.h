@@ -74,9 +74,13 @@ enum RecType : uint32_t { REC_SEG = 0, REC_VRAM = 1, REC_PAL = 2, REC_OAM = 3, R
 // VRAM writes logged one by one between two segments; past this many the next segment is preceded by a
 // whole-VRAM snapshot instead (bulk nametable uploads), which bounds a burst at twice the snapshot size.
 constexpr int VRAM_BURST_MAX = 128;
-// SEG  w0: type | y<<4 | x0<<12 | x1<<21      (visible dots [x0, x1) of line y)
-//      w1: v (16 bits) | fine_x<<16 | render flags<<19
-//      w2: pending-eval bit | eval_y<<1 | oam_addr<<9
+// SEG  w0: type | y0<<4 | x0<<12 | x1<<21     (dots [x0, 256) of line y0, all dots of the lines in between,
+//      w3: y1                                   dots [0, x1) of line y1; [x0, x1) of y0 when y1 == y0)
+//      w1: v at (y0, x0) (16 bits) | fine_x<<16 | render flags<<19
+//      w2: pending-eval bit | eval_y<<1 | oam_addr<<9 | coarse x of t<<17 | nametable-x bit of t<<22
+//      Nothing the CPU does changes a render input inside a segment, so the lines after y0 follow from the
+//      first: v advances by the dot-257 fine-y increment and the dot-258 copy of t's x bits, and each line's
+//      sprite list is the (pending) evaluation of the line before it.
 // VRAM w0: type | index<<4 (11 bits) | value<<16       PAL/OAM the same with 5/8-bit index
 // DMA  w0: type, followed by 16 records holding the whole OAM after the copy
 // LIST w0: type | nsl<<4; w1: sl[0..3]; w2: sl[4..7]
@@ -84,6 +88,24 @@ constexpr int VRAM_BURST_MAX = 128;
 enum : uint32_t { TOUCH_ALL = 1, TOUCH_BG = 2, TOUCH_SPR = 4, TOUCH_VRAM = 8 };
 enum : uint32_t { RF_SHOW_BG = 1, RF_SHOW_SPR = 2, RF_HIDE_BG = 4, RF_HIDE_SPR = 8, RF_LONG = 16,
                   RF_BG_PAGE = 32, RF_SPR_PAGE = 64 };
+
+// v after L fine-y increments (the dot-257 step of nes_core.hpp:318-330 applied L times, closed form). Rows
+// r = coarse_y*8 + fine_y count 0..239 and wrap with a nametable-y toggle; rows 240..255 (coarse y 30/31)
+// run on to 255 and wrap to 0 without the toggle.
+FME_HD uint32_t fine_y_add(uint32_t v, int L) {
+    int r = (int)(((v >> 5) & 31u) * 8u + ((v >> 12) & 7u));
+    uint32_t ny = (v >> 11) & 1u;
+    if (r >= 240) {
+        if (r + L < 256) { r += L; L = 0; }
+        else { L -= 256 - r; r = 0; }
+    }
+    if (r < 240) {
+        r += L;
+        ny ^= (uint32_t)(r / 240) & 1u;
+        r %= 240;
+    }
+    return (v & ~0x7be0u & 0xffffu) | ((uint32_t)(r & 7) << 12) | ((uint32_t)(r >> 3) << 5) | (ny << 11);
+}
 
 // A log slot: frame-start snapshot (VRAM, palette, OAM, sprite-list state) + record stream.
 constexpr int SLOT_HDR_VRAM = 0;

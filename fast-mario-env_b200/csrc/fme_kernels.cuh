@@ -69,7 +69,7 @@ __device__ __forceinline__ void bind_core(Core& c, const Dev& d, uint8_t* sm, in
     c.vram = d.vram + (size_t)e * VRAM_BYTES;
     c.cart.prg = d.prg; c.cart.chr = d.chr;
     for (int i = 0; i < 4; i++) c.cart.nt[i] = d.nt[i];
-    c.rec = nullptr; c.nrec = 0; c.cap = 0; c.seg_open = false; c.seg_w0 = 0; c.status = 0; c.seg_idx = 0; c.seg_reads = 0;
+    c.rec = nullptr; c.nrec = 0; c.cap = 0; c.seg_open = false; c.seg_w0 = 0; c.seg_y1 = 0; c.status = 0; c.seg_idx = 0; c.seg_reads = 0;
     c.vram_burst = 0; c.vram_dirty = false;
 }
 
@@ -138,71 +138,86 @@ __device__ void render_slot(const uint8_t* slot, uint8_t* sm, const Dev& d, bool
     uint32_t skey0 = 0xffffffffu, skey1 = 0, skey2 = 0;        // cached sprite rows of the current line
     uint32_t* srow_s = reinterpret_cast<uint32_t*>(sm + RS_SPR);   // the line's sprite rows (list order)
     uint32_t* sinfo_s = srow_s + 8;
+    // records are read 32 at a time (one coalesced load, lane j holds record wb + j) and broadcast by shuffle
+    int wb = -64;
+    uint4 wv = make_uint4(0u, 0u, 0u, 0u);
     for (int r = 0; r < nrec; r++) {
-        uint4 rec = recs[r];
+        if (r >= wb + 32) {
+            wb = r;
+            if (wb + lane < nrec) wv = recs[wb + lane];
+        }
+        const int jw = r - wb;
+        uint4 rec;
+        rec.x = __shfl_sync(FULL, wv.x, jw); rec.y = __shfl_sync(FULL, wv.y, jw);
+        rec.z = __shfl_sync(FULL, wv.z, jw); rec.w = __shfl_sync(FULL, wv.w, jw);
         uint32_t type = rec.x & 15u;
         if (type == REC_SEG) {
             Seg g = decode_seg(rec);
-            uint32_t nsl, lo, hi;
-            if (g.pend) {
-                uint32_t key = g.ev_y | (g.oam_addr << 8) | ((g.flags & RF_LONG) ? 0x10000u : 0u) | (ver << 17);
-                if (key != lkey) {
-                    int start = (int)(g.oam_addr >> 2);
-                    int range = (g.flags & RF_LONG) ? 16 : 8;
-                    int d0 = (int)g.ev_y - (int)rs.oam[lane * 4];
-                    int d1 = (int)g.ev_y - (int)rs.oam[(lane + 32) * 4];
-                    bool in0 = lane >= start && d0 >= 0 && d0 < range;
-                    bool in1 = lane + 32 >= start && d1 >= 0 && d1 < range;
-                    uint64_t m = (uint64_t)__ballot_sync(FULL, in0) | ((uint64_t)__ballot_sync(FULL, in1) << 32);
-                    uint32_t n = 0, lo_ = 0, hi_ = 0;
-                    while (m && n < 8) {
-                        uint32_t i = (uint32_t)(__ffsll((long long)m) - 1);
-                        m &= m - 1;
-                        if (n < 4) lo_ |= i << (8 * n); else hi_ |= i << (8 * (n - 4));
-                        n++;
+            for (;;) {  // one pass per line of the record
+                uint32_t nsl, lo, hi;
+                if (g.pend) {
+                    uint32_t key = g.ev_y | (g.oam_addr << 8) | ((g.flags & RF_LONG) ? 0x10000u : 0u) | (ver << 17);
+                    if (key != lkey) {
+                        int start = (int)(g.oam_addr >> 2);
+                        int range = (g.flags & RF_LONG) ? 16 : 8;
+                        int d0 = (int)g.ev_y - (int)rs.oam[lane * 4];
+                        int d1 = (int)g.ev_y - (int)rs.oam[(lane + 32) * 4];
+                        bool in0 = lane >= start && d0 >= 0 && d0 < range;
+                        bool in1 = lane + 32 >= start && d1 >= 0 && d1 < range;
+                        uint64_t m = (uint64_t)__ballot_sync(FULL, in0) | ((uint64_t)__ballot_sync(FULL, in1) << 32);
+                        uint32_t n = 0, lo_ = 0, hi_ = 0;
+                        while (m && n < 8) {
+                            uint32_t i = (uint32_t)(__ffsll((long long)m) - 1);
+                            m &= m - 1;
+                            if (n < 4) lo_ |= i << (8 * n); else hi_ |= i << (8 * (n - 4));
+                            n++;
+                        }
+                        lkey = key; lnsl = n; llo = lo_; lhi = hi_;
                     }
-                    lkey = key; lnsl = n; llo = lo_; lhi = hi_;
-                }
-                nsl = lnsl; lo = llo; hi = lhi;
-            } else {
-                nsl = rs.nsl; lo = rs.sl_lo; hi = rs.sl_hi;
-            }
-            const bool spr_on = (g.flags & RF_SHOW_SPR) && nsl;
-            if (spr_on) {
-                uint32_t k0 = (uint32_t)g.y | (nsl << 8) | ((g.flags & (RF_LONG | RF_SPR_PAGE)) << 12) | (ver << 20);
-                if (k0 != skey0 || lo != skey1 || hi != skey2) {
-                    if ((uint32_t)lane < nsl) {
-                        int i = (int)(((lane < 4 ? lo >> (8 * lane) : hi >> (8 * (lane - 4)))) & 0xffu);
-                        srow_s[lane] = sprite_row(rs, g.flags, i, g.y);
-                        sinfo_s[lane] = sprite_info(rs, i);
-                    }
-                    skey0 = k0; skey1 = lo; skey2 = hi;
-                    __syncwarp();
-                }
-            }
-            if (max_mode && first_row < 0) first_row = g.y;
-            const bool to_stage = max_mode && g.y == first_row;
-            const int xa = g.x0 + lane * 8;
-            uint32_t outw[2];
-            render8(rs, g, xa, spr_on ? nsl : 0u, srow_s, sinfo_s, lut, raw, outw);
-            uint8_t* row = to_stage ? stage : fb + g.y * SCREEN_W;
-            if (xa < g.x1) {
-                if (xa + 8 <= g.x1 && (xa & 7) == 0) {
-                    uint2* dst = reinterpret_cast<uint2*>(row + xa);
-                    uint2 nv = make_uint2(outw[0], outw[1]);
-                    if (max_mode && !to_stage) { uint2 ov = *dst; nv.x = __vmaxu4(nv.x, ov.x); nv.y = __vmaxu4(nv.y, ov.y); }
-                    *dst = nv;
+                    nsl = lnsl; lo = llo; hi = lhi;
                 } else {
+                    nsl = rs.nsl; lo = rs.sl_lo; hi = rs.sl_hi;
+                }
+                const bool spr_on = (g.flags & RF_SHOW_SPR) && nsl;
+                if (spr_on) {
+                    uint32_t k0 = (uint32_t)g.y | (nsl << 8) | ((g.flags & (RF_LONG | RF_SPR_PAGE)) << 12) | (ver << 20);
+                    if (k0 != skey0 || lo != skey1 || hi != skey2) {
+                        if ((uint32_t)lane < nsl) {
+                            int i = (int)(((lane < 4 ? lo >> (8 * lane) : hi >> (8 * (lane - 4)))) & 0xffu);
+                            srow_s[lane] = sprite_row(rs, g.flags, i, g.y);
+                            sinfo_s[lane] = sprite_info(rs, i);
+                        }
+                        skey0 = k0; skey1 = lo; skey2 = hi;
+                        __syncwarp();
+                    }
+                }
+                if (max_mode && first_row < 0) first_row = g.y;
+                const bool to_stage = max_mode && g.y == first_row;
+                const int xa = g.x0 + lane * 8;
+                uint32_t outw[2];
+                render8(rs, g, xa, spr_on ? nsl : 0u, srow_s, sinfo_s, lut, raw, outw);
+                uint8_t* row = to_stage ? stage : fb + g.y * SCREEN_W;
+                if (xa < g.x1) {
+                    if (xa + 8 <= g.x1 && (xa & 7) == 0) {
+                        uint2* dst = reinterpret_cast<uint2*>(row + xa);
+                        uint2 nv = make_uint2(outw[0], outw[1]);
+                        if (max_mode && !to_stage) { uint2 ov = *dst; nv.x = __vmaxu4(nv.x, ov.x); nv.y = __vmaxu4(nv.y, ov.y); }
+                        *dst = nv;
+                    } else {
 #pragma unroll
-                    for (int j = 0; j < 8; j++) {
-                        const int xx = xa + j;
-                        if (xx < g.x1) {
-                            uint8_t val = (uint8_t)(outw[j >> 2] >> (8 * (j & 3)));
-                            if (max_mode && !to_stage) { uint8_t o = row[xx]; row[xx] = val > o ? val : o; }
-                            else row[xx] = val;
+                        for (int j = 0; j < 8; j++) {
+                            const int xx = xa + j;
+                            if (xx < g.x1) {
+                                uint8_t val = (uint8_t)(outw[j >> 2] >> (8 * (j & 3)));
+                                if (max_mode && !to_stage) { uint8_t o = row[xx]; row[xx] = val > o ? val : o; }
+                                else row[xx] = val;
+                            }
                         }
                     }
                 }
+                if (g.y >= g.y1) break;
+                seg_next_line(g);
+                __syncwarp();
             }
         } else if (type == REC_DMA) {
             if (r + 16 >= nrec) break;  // truncated payload (the frame overflowed its log; status says so)

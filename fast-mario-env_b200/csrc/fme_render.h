@@ -56,18 +56,44 @@ FME_HD uint32_t r_pb_read(const RState& s, uint32_t addr) {
     return 0;
 }
 
-// segment descriptor decoded once per record
+FME_HD int inc_count_fx(uint32_t fine_x, int x0, int x1) {
+    int r = (7 - (int)fine_x) & 7;
+    return (x1 - r + 7) / 8 - (x0 - r + 7) / 8;
+}
+
+// One line of a segment record: decode_seg gives its first line, seg_next_line steps to the next one.
 struct Seg {
-    int y, x0, x1;
+    int y, x0, x1;          // this line and its dots [x0, x1)
     uint32_t v, fine_x, flags;
     uint32_t pend, ev_y, oam_addr;
+    int y1, xe;             // last line of the record and its end dot
+    uint32_t tx;            // t's x bits (coarse x, nametable x), copied into v at dot 258
 };
 FME_HD Seg decode_seg(uint4 r) {
     Seg s;
-    s.y = (int)((r.x >> 4) & 0xffu); s.x0 = (int)((r.x >> 12) & 0x1ffu); s.x1 = (int)((r.x >> 21) & 0x1ffu);
+    s.y = (int)((r.x >> 4) & 0xffu); s.x0 = (int)((r.x >> 12) & 0x1ffu); s.xe = (int)((r.x >> 21) & 0x1ffu);
     s.v = r.y & 0xffffu; s.fine_x = (r.y >> 16) & 7u; s.flags = (r.y >> 19) & 0x7fu;
     s.pend = r.z & 1u; s.ev_y = (r.z >> 1) & 0xffu; s.oam_addr = (r.z >> 9) & 0xffu;
+    s.tx = ((r.z >> 17) & 0x1fu) | (((r.z >> 22) & 1u) << 10);
+    s.y1 = (int)(r.w & 0xffu) > s.y ? (int)(r.w & 0xffu) : s.y;
+    s.x1 = s.y1 == s.y ? s.xe : 256;
     return s;
+}
+// v from the line's first dot to the next line's dot 0 (nes_core.hpp:310-334: coarse-x increments of the
+// remaining dots, fine-y at 257, copy of t's x bits at 258), and that line's list (evaluation of this one).
+FME_HD void seg_next_line(Seg& g) {
+    if (g.flags & RF_SHOW_BG) {
+        uint32_t v = g.v;
+        const int n = inc_count_fx(g.fine_x, g.x0, 256);
+        uint32_t tot = (v & 0x1fu) + (uint32_t)n;
+        v = (v & ~0x1fu & 0xffffu) | (tot & 31u);
+        if ((tot >> 5) & 1u) v ^= 0x0400u;
+        v = fine_y_add(v, 1);
+        if (g.flags & RF_SHOW_SPR) v = (v & ~0x041fu & 0xffffu) | g.tx;
+        g.v = v;
+    }
+    g.pend = 1u; g.ev_y = (uint32_t)g.y;
+    g.y++; g.x0 = 0; g.x1 = g.y == g.y1 ? g.xe : 256;
 }
 
 // v after n coarse-x increments (nes_core.hpp:310-315 applied n times in closed form)
@@ -78,10 +104,6 @@ FME_HD uint32_t v_after(uint32_t v, int n) {
     // each wrap of the 5-bit coarse x toggles the nametable bit
     if (((tot >> 5) & 1u)) r ^= 0x0400u;
     return r;
-}
-FME_HD int inc_count_fx(uint32_t fine_x, int x0, int x1) {
-    int r = (7 - (int)fine_x) & 7;
-    return (x1 - r + 7) / 8 - (x0 - r + 7) / 8;
 }
 
 // 2-bit sprite pattern (exact integer semantics of nes_core.hpp:368-387) using the segment's flags

@@ -824,6 +824,47 @@ struct Core {
         return skip;
     }
 
+    // ================================================================ sprite-0 busy-wait
+    // The instruction at pc (executing at iteration J) may open a loop that polls $2002 until bit 6 (the
+    // sprite-0 flag) changes: `BIT $2002 / BVC|BVS *-3` or `LDA $2002 / AND #$40 / BEQ|BNE *-5`. Once vblank
+    // is clear and the address latch reset, another read of $2002 only catches the PPU up, and the loop's
+    // other instructions are plain register work that the exiting iteration overwrites (A, N, V, Z). So the
+    // iterations whose read still sees the waiting value are replaced by their PPU catch-ups; the read that
+    // ends the loop runs as usual. Iterations are skipped only while the next read stays before the NMI
+    // pre-sync and the frame end, where the frame loop has work of its own. Returns the skipped cycles.
+    FME_NI int32_t poll_skip(int32_t J, uint32_t opc) {
+        if (vblank || !first_write || pc < 0x8000u || pc > 0xfff8u) return 0;
+        if (prg(pc + 1) != 0x02u || prg(pc + 2) != 0x20u) return 0;
+        uint32_t br, br_pc, exit_bit;
+        int32_t it;
+        if (opc == 0x2Cu) {                                   // BIT $2002 / BVC|BVS back
+            br = prg(pc + 3);
+            if ((br != 0x50u && br != 0x70u) || prg(pc + 4) != 0xFBu) return 0;
+            exit_bit = br == 0x50u ? 1u : 0u;
+            br_pc = pc + 3;
+            it = (int32_t)d_cycles(FME_DTAB(0x2Cu));
+        } else {                                              // LDA $2002 / AND #$40 / BEQ|BNE back
+            if (prg(pc + 3) != 0x29u || prg(pc + 4) != 0x40u) return 0;
+            br = prg(pc + 5);
+            if ((br != 0xF0u && br != 0xD0u) || prg(pc + 6) != 0xF9u) return 0;
+            exit_bit = br == 0xF0u ? 1u : 0u;
+            br_pc = pc + 5;
+            it = (int32_t)d_cycles(FME_DTAB(0xADu)) + (int32_t)d_cycles(FME_DTAB(0x29u));
+        }
+        it += (int32_t)d_cycles(FME_DTAB(br)) + 1 + ((((br_pc + 2u) ^ pc) & 0xff00u) ? 2 : 0);  // taken branch
+        int32_t D = 0;
+        for (;;) {
+            const int32_t Jk = J + D, Jn = Jk + it;
+            if (3 * (Jn + 1) >= nmi_thresh || Jn >= FRAME_ITERS) break;
+            cur = Jk;
+            sync();                                           // the catch-up of this iteration's read
+            if (s0hit == exit_bit) break;                     // this read ends the loop
+            D += it;
+        }
+        cur = J + D;
+        return D;
+    }
+
     // ================================================================ frame driver (nes_core.hpp:1166-1204)
     // Run until the instruction boundary test. Returns false once exec_at reached the frame end.
     // One call = one executed instruction (or an NMI / idle-loop skip).
@@ -852,7 +893,8 @@ struct Core {
             }
         }
         cur = J;
-        int32_t S = execute_op(opc != 0x100u ? opc : rd(pc));
+        int32_t D = (opc == 0x2Cu || opc == 0xADu) ? poll_skip(J, opc) : 0;
+        int32_t S = D + execute_op(opc != 0x100u ? opc : rd(pc));
         exec_at = J + (S >= 1 ? S : 1);
         zero_skip = S <= 0;
         return true;

@@ -26,7 +26,8 @@ FME_NI void slow_presync(Core& c, int32_t J) {
 }
 FME_NI int32_t slow_execute(Core& c, int32_t J, uint32_t opc) {
     c.cur = J;
-    return opc <= 0xffu ? c.execute_op(opc) : c.execute_op(c.rd(c.pc));
+    const int32_t D = (opc == 0x2Cu || opc == 0xADu) ? c.poll_skip(J, opc) : 0;  // sets cur = J + D
+    return D + (opc <= 0xffu ? c.execute_op(opc) : c.execute_op(c.rd(c.pc)));
 }
 
 struct Fast {

@@ -104,7 +104,8 @@ constexpr int RS_STAGE = RS_OAM + OAM_BYTES;     // one staged row (256)
 constexpr int RS_OBS = RS_STAGE + SCREEN_W;      // 84 x 84 result
 constexpr int RS_LUT = RS_OBS + OBS_BYTES;       // 256-entry gray LUT (identity for raw screens)
 constexpr int RS_SPR = RS_LUT + 256;             // 16 words: sprite rows and infos of the current line
-constexpr int RS_END = RS_SPR + 64;
+constexpr int RS_GV = RS_SPR + 64;               // 32 output values, one per palette address
+constexpr int RS_END = RS_GV + 32;
 static_assert(RS_END <= SLAB_BYTES, "render scratch must fit the slab region");
 
 // Replay one logged frame into the framebuffer. raw: palette values (screen) instead of gray.
@@ -131,6 +132,12 @@ __device__ void render_slot(const uint8_t* slot, uint8_t* sm, const Dev& d, bool
     rs.nsl = lw[0] & 0xffu; rs.sl_lo = lw[1]; rs.sl_hi = lw[2];
     const int nrec = (int)lw[3] < d.log_cap ? (int)lw[3] : d.log_cap;
     const uint4* recs = reinterpret_cast<const uint4*>(slot + SLOT_HDR_BYTES);
+    uint8_t* gv = sm + RS_GV;
+    __syncwarp();
+    {
+        const uint32_t pv = rs.pal[lane];
+        gv[lane] = raw ? (uint8_t)pv : lut[pv];
+    }
     __syncwarp();
     int first_row = -1;
     uint32_t ver = 0;                                   // bumps on every content change (VRAM/palette/OAM)
@@ -195,7 +202,7 @@ __device__ void render_slot(const uint8_t* slot, uint8_t* sm, const Dev& d, bool
                 const bool to_stage = max_mode && g.y == first_row;
                 const int xa = g.x0 + lane * 8;
                 uint32_t outw[2];
-                render8(rs, g, xa, spr_on ? nsl : 0u, srow_s, sinfo_s, lut, raw, outw);
+                render8(rs, g, xa, spr_on ? nsl : 0u, srow_s, sinfo_s, gv, outw);
                 uint8_t* row = to_stage ? stage : fb + g.y * SCREEN_W;
                 if (xa < g.x1) {
                     if (xa + 8 <= g.x1 && (xa & 7) == 0) {
@@ -239,7 +246,7 @@ __device__ void render_slot(const uint8_t* slot, uint8_t* sm, const Dev& d, bool
             if (lane == 0) {
                 uint32_t idx = (rec.x >> 4) & 0x7ffu, val = (rec.x >> 16) & 0xffu;
                 if (type == REC_VRAM) rs.vram[idx] = (uint8_t)val;
-                else if (type == REC_PAL) rs.pal[idx & 31u] = (uint8_t)val;
+                else if (type == REC_PAL) { rs.pal[idx & 31u] = (uint8_t)val; gv[idx & 31u] = raw ? (uint8_t)val : lut[val]; }
                 else if (type == REC_OAM) rs.oam[idx & 255u] = (uint8_t)val;
             }
             ver++;

@@ -269,26 +269,38 @@ FME_HD void bg_tile(const RState& rs, uint32_t v, uint32_t bg_page, uint32_t& lo
     at = (attr >> (((v >> 4) & 4u) | (v & 2u))) & 3u;
 }
 
+// bit k of n (k < 4) -> byte k
+FME_HD uint32_t expand4(uint32_t n) { return (n * 0x00204081u) & 0x01010101u; }
+
 // The 8 output values of dots xa..xa+7 of segment g (bytes j of out[0..1]; dots outside the segment are
-// computed but must not be stored). srow/sinfo: the line's sprite rows (list order), nsl of them.
+// computed but must not be stored). srow/sinfo: the line's sprite rows (list order), nsl of them. gv: the
+// output value of each of the 32 palette addresses (palette entry, through the gray LUT unless raw).
+// Per-dot decisions of nes_core.hpp:422-513 are made on 8-bit planes (bit 7-j = dot xa+j): background
+// pattern bits and palette select, left-edge hiding, first opaque sprite of the list, and its priority.
 FME_HD void render8(const RState& rs, const Seg& g, int xa, uint32_t nsl, const uint32_t* srow, const uint32_t* sinfo,
-                    const uint8_t* lut, bool raw, uint32_t* out) {
-    uint32_t wlo = 0, whi = 0, at0 = 0, at1 = 0, s = 0;
+                    const uint8_t* gv, uint32_t* out) {
+    const uint32_t keep = xa >= 8 ? 0xffu : (1u << xa) - 1u;   // dots at x >= 8 (for left-edge hiding)
+    uint32_t wlo = 0, whi = 0, am0 = 0, am1 = 0;
     if (g.flags & RF_SHOW_BG) {
         const int tx0 = ((int)g.fine_x + g.x0) >> 3;
         const int t0 = ((int)g.fine_x + xa) >> 3;
-        s = ((uint32_t)g.fine_x + (uint32_t)xa) & 7u;
+        const uint32_t s = ((uint32_t)g.fine_x + (uint32_t)xa) & 7u;
         const uint32_t bgp = (g.flags & RF_BG_PAGE) ? 1u : 0u;
-        uint32_t lo0, hi0, lo1 = 0, hi1 = 0;
+        uint32_t lo0, hi0, at0, lo1 = 0, hi1 = 0, at1;
         bg_tile(rs, v_after(g.v, t0 - tx0), bgp, lo0, hi0, at0);
         at1 = at0;
         if (s) bg_tile(rs, v_after(g.v, t0 + 1 - tx0), bgp, lo1, hi1, at1);
         wlo = (((lo0 << 8) | lo1) >> (8u - s)) & 0xffu;
         whi = (((hi0 << 8) | hi1) >> (8u - s)) & 0xffu;
+        const uint32_t first = (0xffu << s) & 0xffu;           // dots of the first tile
+        am0 = ((at0 & 1u) ? first : 0u) | ((at1 & 1u) ? (~first & 0xffu) : 0u);
+        am1 = ((at0 & 2u) ? first : 0u) | ((at1 & 2u) ? (~first & 0xffu) : 0u);
+        if (g.flags & RF_HIDE_BG) { wlo &= keep; whi &= keep; }
     }
-    uint32_t filled = 0, front_m = 0, sc0 = 0, sc1 = 0;  // sprite palette address of dot j in byte j of sc0|sc1
-    const bool spr_on = (g.flags & RF_SHOW_SPR) && nsl;
-    if (spr_on) {
+    const uint32_t bo = wlo | whi;                               // opaque background dots
+    am0 &= bo; am1 &= bo;
+    uint32_t filled = 0, front_m = 0, p0 = 0, p1 = 0, q0 = 0, q1 = 0;
+    if ((g.flags & RF_SHOW_SPR) && nsl) {
         for (uint32_t k = 0; k < nsl; k++) {
             const uint32_t inf = sinfo[k];
             const int o = xa - (int)(inf & 0xffu);
@@ -296,33 +308,28 @@ FME_HD void render8(const RState& rs, const Seg& g, int xa, uint32_t nsl, const 
             const uint32_t rl = srow[k] & 0xffu, rh = (srow[k] >> 8) & 0xffu;
             const uint32_t al = o >= 0 ? (rl << o) & 0xffu : rl >> (-o);
             const uint32_t ah = o >= 0 ? (rh << o) & 0xffu : rh >> (-o);
-            const uint32_t nw = (al | ah) & ~filled;
+            const uint32_t nw = (al | ah) & ~filled;             // dots this sprite is the first opaque one
             if (!nw) continue;
             filled |= nw;
             if (inf & (1u << 13)) front_m |= nw;
-            const uint32_t cb = (inf >> 8) & 0x1fu;
-            for (int j = 0; j < 8; j++) {
-                if (nw & (0x80u >> j)) {
-                    uint32_t c = (((al >> (7 - j)) & 1u) | (((ah >> (7 - j)) & 1u) << 1)) | cb;
-                    if (j < 4) sc0 |= c << (8 * j); else sc1 |= c << (8 * (j - 4));
-                }
-            }
+            p0 |= al & nw; p1 |= ah & nw;
+            if (inf & (1u << 10)) q0 |= nw;                     // sprite palette bits (address bits 2, 3)
+            if (inf & (1u << 11)) q1 |= nw;
         }
+        if (g.flags & RF_HIDE_SPR) filled &= keep;
     }
-    out[0] = 0; out[1] = 0;
-    for (int j = 0; j < 8; j++) {
-        const int xx = xa + j;
-        uint32_t pa = 0;
-        uint32_t b = ((wlo >> (7 - j)) & 1u) | (((whi >> (7 - j)) & 1u) << 1);
-        if (b) pa = b | ((((uint32_t)j < 8u - s) ? at0 : at1) << 2);
-        if ((g.flags & RF_HIDE_BG) && xx < 8) pa = 0;
-        if ((filled & (0x80u >> j)) && !((g.flags & RF_HIDE_SPR) && xx < 8)) {
-            if (!(pa & 3u) || (front_m & (0x80u >> j))) pa = ((j < 4 ? sc0 >> (8 * j) : sc1 >> (8 * (j - 4)))) & 0x1fu;
-        }
-        uint32_t px = rs.pal[pa];
-        uint32_t val = raw ? px : lut[px];
-        out[j >> 2] |= val << (8 * (j & 3));
-    }
+    const uint32_t W = filled & (~bo | front_m);               // dots where the sprite is drawn
+    const uint32_t P0 = brev8((wlo & ~W) | (p0 & W)), P1 = brev8((whi & ~W) | (p1 & W));
+    const uint32_t P2 = brev8((am0 & ~W) | (q0 & W)), P3 = brev8((am1 & ~W) | (q1 & W)), P4 = brev8(W);
+    // palette address of dot j in byte j
+    const uint32_t alo = expand4(P0 & 15u) | (expand4(P1 & 15u) << 1) | (expand4(P2 & 15u) << 2) |
+                         (expand4(P3 & 15u) << 3) | (expand4(P4 & 15u) << 4);
+    const uint32_t ahi = expand4(P0 >> 4) | (expand4(P1 >> 4) << 1) | (expand4(P2 >> 4) << 2) |
+                         (expand4(P3 >> 4) << 3) | (expand4(P4 >> 4) << 4);
+    out[0] = (uint32_t)gv[alo & 0xffu] | ((uint32_t)gv[(alo >> 8) & 0xffu] << 8) |
+             ((uint32_t)gv[(alo >> 16) & 0xffu] << 16) | ((uint32_t)gv[alo >> 24] << 24);
+    out[1] = (uint32_t)gv[ahi & 0xffu] | ((uint32_t)gv[(ahi >> 8) & 0xffu] << 8) |
+             ((uint32_t)gv[(ahi >> 16) & 0xffu] << 16) | ((uint32_t)gv[ahi >> 24] << 24);
 }
 
 }  // namespace fme

@@ -143,6 +143,55 @@ def cpu_baseline(rom, args, seconds=12.0):
                       f"(oracle/_ref/libfastmario.so, {cores} threads), same config"}
 
 
+def reference_cuda(rom, E, steps, warmup, dev):
+    """The reference's own GPU engine (CudaVecEnv, one thread per env, NVRTC-compiled from baseline/_ref) and
+    this engine, both at maxpool=False (the only setting the reference's GPU path supports), same levels,
+    seeds and actions otherwise. Device-timed steps with the actions already on the device."""
+    import torch
+    ref_dir = os.path.join(ROOT, "baseline", "_ref")
+    if not os.path.isdir(os.path.join(ref_dir, "fast_mario_env")):
+        return {"unavailable": "baseline/_ref not installed"}
+    sys.path.insert(0, ref_dir)
+    try:
+        from fast_mario_env.cuda.vec_env import CudaVecEnv as RefCuda
+    except Exception as e:  # noqa: BLE001
+        return {"unavailable": f"reference CudaVecEnv import failed: {e}"}
+    fme = load_package()
+    g = torch.Generator(device=dev)
+    g.manual_seed(4321)
+    acts = torch.randint(0, 7, (warmup + steps, E), dtype=torch.int64, device=dev, generator=g)
+    out = {"config": "config1 with maxpool=False", "n_envs": E, "steps": steps}
+    with tempfile.NamedTemporaryFile(suffix=".nes", delete=False) as f:
+        f.write(rom)
+        rom_path = f.name
+    try:
+        for name, make in (("reference_cudavecenv", lambda: RefCuda(level_names(E), E, seed=0, sticky=0.25, noop_max=30,
+                                                                     max_steps=2000, skip=4, device=dev, rom_path=rom_path)),
+                           ("ours", lambda: fme.CudaVecEnv(level_names(E), E, seed=0, sticky=0.25, noop_max=30,
+                                                           max_steps=2000, skip=4, frame_stack=4, maxpool=False,
+                                                           device=dev, rom=rom))):
+            env = make()
+            env.reset()
+            for t in range(warmup):
+                env.step(acts[t])
+            torch.cuda.synchronize(dev)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for t in range(warmup, warmup + steps):
+                env.step(acts[t])
+            e1.record()
+            torch.cuda.synchronize(dev)
+            ms = e0.elapsed_time(e1) / steps
+            out[name] = {"value": E / (ms / 1000.0), "ms_per_step": ms, "unit": UNIT}
+            if hasattr(env, "close"):
+                env.close()
+            del env
+            torch.cuda.empty_cache()
+    finally:
+        os.unlink(rom_path)
+    return out
+
+
 def run_reference(args, rank):
     if rank != 0:
         return
@@ -169,6 +218,8 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--ref-gpu", action="store_true",
+                    help="also time the reference's CudaVecEnv (baseline/_ref) against this engine at maxpool=False")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
@@ -265,12 +316,17 @@ def main():
     cb = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cb = cpu_baseline(rom, args)
+    ref_cuda = None
+    if args.ref_gpu and rank == 0 and world == 1:
+        ref_cuda = reference_cuda(rom, E, args.steps, args.warmup, dev)
     if rank == 0:
         line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
                 "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak",
                 "vs_baseline": None, "dtype": "u8", "data": "synthetic", "config": workload(args),
-                "parallelism": f"env shards by env_offset x{world}, no collective", "gpu_launches": args.steps,
+                "parallelism": f"env shards by env_offset x{world}, no collective", "gpu_launches": 2 * args.steps,
                 "roofline": roofline, "cpu_baseline": cb, "e2e": e2e, "clocks": clk}
+        if ref_cuda is not None:
+            line["reference_cuda"] = ref_cuda
         print(json.dumps(line))
     env.close()
     if dist:

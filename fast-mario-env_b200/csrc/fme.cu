@@ -105,7 +105,7 @@ __global__ void __launch_bounds__(32) k_boot(BootParams P) {
     for (int j = 0; j < 32; j++) {
         int lj = g * 32 + j;
         if (lj >= P.n_levels) break;
-        render_slot(d.logs + slot_off(lj, 0, d.log_cap), sm, d, false, false, lane);
+        render_slot(d.logs + slot_off(lj, 0, d.log_cap), full_layout(sm), d, false, false, lane);
         resize_fb(sm, lane);
         wcopy16(P.obs0 + (size_t)lj * OBS_BYTES, sm + RS_OBS, OBS_BYTES, lane);
         __syncwarp();
@@ -230,10 +230,34 @@ __global__ void __launch_bounds__(32) k_step(StepParams P) {
     copy_slab(d.slab + (size_t)g * SLAB_BYTES, sm, lane);
     __syncwarp();
 
-    // ---- render, resize, frame stack (warp-cooperative, one env at a time)
-    load_lut(sm, d.lut, lane);
     const uint32_t summary = (active ? 1u : 0u) | (pooled ? 2u : 0u) | ((uint32_t)cur_slot << 2) | (ended ? 8u : 0u);
     const int K = P.frame_stack;
+    if (P.jobs) {
+        // ---- the frames are drawn by k_render: shift the stacks (and stage the finished episodes' stacks and
+        // the reset frames) so that it only has to write frame K-1 of obs or final_obs
+        if (active) P.jobs[e] = summary;
+        for (int j = 0; j < 32; j++) {
+            const uint32_t sj = __shfl_sync(FULL, summary, j);
+            const int cij = __shfl_sync(FULL, reset_ci, j);
+            if (!(sj & 1u)) continue;
+            const int ej = g * 32 + j;
+            uint8_t* o = P.obs + (size_t)ej * K * OBS_BYTES;
+            if (K > 1) wmove16(o, o + OBS_BYTES, (K - 1) * OBS_BYTES, lane);
+            __syncwarp();
+            if (sj & 8u) {
+                uint8_t* f = P.fin + (size_t)ej * K * OBS_BYTES;
+                if (K > 1) wcopy16(f, o, (K - 1) * OBS_BYTES, lane);
+                __syncwarp();
+                if (K > 1) wzero16(o, (K - 1) * OBS_BYTES, lane);
+                wcopy16(o + (size_t)(K - 1) * OBS_BYTES, P.cache.obs + (size_t)cij * OBS_BYTES, OBS_BYTES, lane);
+            }
+            __syncwarp();
+        }
+        return;
+    }
+
+    // ---- render, resize, frame stack (warp-cooperative, one env at a time)
+    load_lut(sm, d.lut, lane);
     for (int j = 0; j < 32; j++) {
         uint32_t sj = __shfl_sync(FULL, summary, j);
         int cij = __shfl_sync(FULL, reset_ci, j);
@@ -245,7 +269,7 @@ __global__ void __launch_bounds__(32) k_step(StepParams P) {
             uint8_t* dst = P.out_obs + (size_t)cij * OBS_BYTES;
             if (dj) wcopy16(dst, P.level_obs0 + (size_t)(cij / (P.noop_max + 1)) * OBS_BYTES, OBS_BYTES, lane);
             else {
-                render_slot(d.logs + slot_off(ej, cs, cap), sm, d, false, false, lane);
+                render_slot(d.logs + slot_off(ej, cs, cap), full_layout(sm), d, false, false, lane);
                 resize_fb(sm, lane);
                 wcopy16(dst, sm + RS_OBS, OBS_BYTES, lane);
             }
@@ -253,10 +277,10 @@ __global__ void __launch_bounds__(32) k_step(StepParams P) {
             continue;
         }
         if (pj) {
-            render_slot(d.logs + slot_off(ej, cs ^ 1, cap), sm, d, false, false, lane);
-            render_slot(d.logs + slot_off(ej, cs, cap), sm, d, false, true, lane);
+            render_slot(d.logs + slot_off(ej, cs ^ 1, cap), full_layout(sm), d, false, false, lane);
+            render_slot(d.logs + slot_off(ej, cs, cap), full_layout(sm), d, false, true, lane);
         } else {
-            render_slot(d.logs + slot_off(ej, cs, cap), sm, d, false, false, lane);
+            render_slot(d.logs + slot_off(ej, cs, cap), full_layout(sm), d, false, false, lane);
         }
         resize_fb(sm, lane);
         uint8_t* o = P.obs + (size_t)ej * K * OBS_BYTES;
@@ -274,6 +298,59 @@ __global__ void __launch_bounds__(32) k_step(StepParams P) {
         }
         __syncwarp();
     }
+}
+
+// ---- k_render: the new frame of every env, one CTA (one warp) per (env, band of 60 screen rows).
+// A band's 60 rows are exactly the source rows of 21 output rows (240/84 = 20/7), so each CTA replays the
+// env's log(s) drawing only its rows, resizes them and writes its 21 rows of the stacked frame. The small
+// shared-memory footprint (about 20 KB) lets 10 CTAs share an SM and hide each other's latencies.
+constexpr int BAND_ROWS = 60, BAND_OUT = 21, NBANDS = SCREEN_H / BAND_ROWS;
+constexpr int RB_FB = 0;
+constexpr int RB_VRAM = RB_FB + BAND_ROWS * SCREEN_W;
+constexpr int RB_PAL = RB_VRAM + VRAM_BYTES;
+constexpr int RB_OAM = RB_PAL + PAL_BYTES;
+constexpr int RB_STAGE = RB_OAM + OAM_BYTES;
+constexpr int RB_OBS = RB_STAGE + SCREEN_W;
+constexpr int RB_LUT = RB_OBS + (BAND_OUT * OBS + 15) / 16 * 16;
+constexpr int RB_SPR = RB_LUT + 256;
+constexpr int RB_GV = RB_SPR + 64;
+constexpr int RB_BYTES = RB_GV + 32;
+static_assert(NBANDS * BAND_OUT == OBS && BAND_ROWS * OBS == BAND_OUT * SCREEN_H, "bands must align with the taps");
+static_assert(RB_VRAM % 16 == 0 && RB_OAM % 16 == 0 && RB_LUT % 16 == 0 && RB_OBS % 4 == 0, "alignment");
+
+struct RenderParams {
+    Dev d;
+    const uint32_t* jobs;
+    uint8_t* obs; uint8_t* fin;
+    int frame_stack;
+};
+__global__ void __launch_bounds__(32) k_render(RenderParams P) {
+    extern __shared__ __align__(16) uint8_t sm[];
+    const int lane = threadIdx.x;
+    const int e = blockIdx.x / NBANDS, band = blockIdx.x % NBANDS;
+    const Dev& d = P.d;
+    if (e >= d.n) return;
+    const uint32_t job = P.jobs[e];
+    if (!(job & 1u)) return;
+    RLayout L;
+    L.fb = sm + RB_FB; L.vram = sm + RB_VRAM; L.pal = sm + RB_PAL; L.oam = sm + RB_OAM; L.stage = sm + RB_STAGE;
+    L.lut = sm + RB_LUT; L.spr = reinterpret_cast<uint32_t*>(sm + RB_SPR); L.gv = sm + RB_GV;
+    L.row_lo = band * BAND_ROWS; L.row_hi = L.row_lo + BAND_ROWS;
+    if (lane < 16) reinterpret_cast<uint4*>(sm + RB_LUT)[lane] = reinterpret_cast<const uint4*>(d.lut)[lane];
+    __syncwarp();
+    const int cs = (int)((job >> 2) & 1u);
+    const int cap = d.log_cap;
+    if (job & 2u) {
+        render_slot(d.logs + slot_off(e, cs ^ 1, cap), L, d, false, false, lane);
+        render_slot(d.logs + slot_off(e, cs, cap), L, d, false, true, lane);
+    } else {
+        render_slot(d.logs + slot_off(e, cs, cap), L, d, false, false, lane);
+    }
+    resize_band(L.fb, L.row_lo, band * BAND_OUT, band * BAND_OUT + BAND_OUT, sm + RB_OBS, lane);
+    const int K = P.frame_stack;
+    uint8_t* dst = ((job & 8u) ? P.fin : P.obs) + ((size_t)e * K + (K - 1)) * OBS_BYTES + (size_t)band * BAND_OUT * OBS;
+    const uint32_t* src = reinterpret_cast<const uint32_t*>(sm + RB_OBS);
+    for (int i = lane; i < BAND_OUT * OBS / 4; i += 32) reinterpret_cast<uint32_t*>(dst)[i] = src[i];
 }
 
 // Every env at its level snapshot (Env::init -> restore_backup, fastmario.cpp:285-295), RNG from the host.
@@ -399,7 +476,7 @@ __global__ void __launch_bounds__(32) k_raw(RawParams P) {
     for (int j = 0; j < 32; j++) {
         int ej = g * 32 + j;
         if (ej >= d.n) break;
-        render_slot(d.logs + slot_off(ej, 0, d.log_cap), sm, d, true, false, lane);
+        render_slot(d.logs + slot_off(ej, 0, d.log_cap), full_layout(sm), d, true, false, lane);
         wcopy16(P.screens + (size_t)ej * SCREEN_W * SCREEN_H, sm + RS_FB, SCREEN_W * SCREEN_H, lane);
         __syncwarp();
     }
@@ -492,6 +569,9 @@ int ensure_constants(int device) {
     build_dtab(dt);
     AreaTabs T;
     if (!build_area(T)) return fail(FME_E_ARG, "area table has more than 6 taps");
+    for (int dy = 0; dy < OBS; dy++)  // k_render: every tap of an output row lies in that row's band
+        for (int m = 0; m < 6 && T.yw[m][dy] != 0.f; m++)
+            if (T.ys[m][dy] / BAND_ROWS != dy / BAND_OUT) return fail(FME_E_ARG, "area taps cross a render band");
     CK(cudaMemcpyToSymbol(c_dtab, dt, sizeof(dt)));
     CK(cudaMemcpyToSymbol(c_area, &T, sizeof(T)));
     const int smem = SLAB_BYTES;
@@ -500,6 +580,7 @@ int ensure_constants(int device) {
     CK(cudaFuncSetAttribute(k_raw, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
     CK(cudaFuncSetAttribute(k_resize, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
     CK(cudaFuncSetAttribute(k_power, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    CK(cudaFuncSetAttribute(k_render, cudaFuncAttributeMaxDynamicSharedMemorySize, RB_BYTES));
     g_const_done[device] = true;
     return FME_OK;
 }
@@ -584,6 +665,7 @@ struct FmeEnv {
     uint8_t* d_cache_img = nullptr;
     uint8_t* d_cache_obs = nullptr;
     int32_t* d_cache_meta = nullptr;
+    uint32_t* d_jobs = nullptr;   // per-env render job of the last step (k_step -> k_render)
     FmeBuffers buf{};
     bool bound = false;
     uint64_t sticky_thr = 0;
@@ -608,7 +690,7 @@ static void free_env(FmeEnv* v) {
     cudaFree(v->d_prg); cudaFree(v->d_chr); cudaFree(v->d_lut); cudaFree(v->d_err);
     v->env.release();
     cudaFree(v->d_level_img); cudaFree(v->d_level_meta); cudaFree(v->d_obs0);
-    cudaFree(v->d_cache_img); cudaFree(v->d_cache_obs); cudaFree(v->d_cache_meta);
+    cudaFree(v->d_cache_img); cudaFree(v->d_cache_obs); cudaFree(v->d_cache_meta); cudaFree(v->d_jobs);
     delete v;
 }
 
@@ -670,6 +752,7 @@ static int create_impl(const FmeConfig* cfg, const uint8_t* rom, int64_t rom_len
     CK(cudaMalloc(&v->d_chr, 0x2000));
     CK(cudaMalloc(&v->d_lut, 256));
     CK(cudaMalloc(&v->d_err, 4));
+    CK(cudaMalloc(&v->d_jobs, (size_t)(C.n_envs + 31) / 32 * 32 * 4));
     CK(cudaMemcpy(v->d_prg, prg.data(), 0x8000, cudaMemcpyHostToDevice));
     CK(cudaMemcpy(v->d_chr, chr.data(), 0x2000, cudaMemcpyHostToDevice));
     CK(cudaMemcpy(v->d_lut, gray_lut, 256, cudaMemcpyHostToDevice));
@@ -810,8 +893,15 @@ static int launch_step_like(FmeEnv* v, const int64_t* d_actions, void* stream, b
     P.trunc = v->buf.trunc; P.info = v->buf.info; P.ep_ret = v->buf.ep_ret; P.ep_len = v->buf.ep_len;
     cudaStream_t s = (cudaStream_t)stream;
     const int groups = (v->n + 31) / 32;
-    if (reset) k_reset<<<groups, 32, 0, s>>>(P);
-    else k_step<<<groups, 32, SLAB_BYTES, s>>>(P);
+    if (reset) {
+        k_reset<<<groups, 32, 0, s>>>(P);
+    } else {
+        P.jobs = v->d_jobs;
+        k_step<<<groups, 32, SLAB_BYTES, s>>>(P);
+        RenderParams R;
+        R.d = d; R.jobs = v->d_jobs; R.obs = P.obs; R.fin = P.fin; R.frame_stack = P.frame_stack;
+        k_render<<<(unsigned)v->n * NBANDS, 32, RB_BYTES, s>>>(R);
+    }
     CK(cudaGetLastError());
     return FME_OK;
 }

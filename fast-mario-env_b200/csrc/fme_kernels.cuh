@@ -52,6 +52,8 @@ struct StepParams {
     int32_t* ep_len;
     Cache cache;
     int n_levels;
+    // MODE_STEP with k_render: per-env render job word (bit 0 active, 1 pooled, 2 slot, 3 episode ended)
+    uint32_t* jobs;
     // MODE_NOOP: where to write the cache entry for this noop step
     uint8_t* out_img; uint8_t* out_obs; int32_t* out_meta; int noop_j;
     const uint8_t* level_img; const uint8_t* level_obs0; const int32_t* level_meta;  // backups (x0, t0)
@@ -108,17 +110,33 @@ constexpr int RS_GV = RS_SPR + 64;               // 32 output values, one per pa
 constexpr int RS_END = RS_GV + 32;
 static_assert(RS_END <= SLAB_BYTES, "render scratch must fit the slab region");
 
-// Replay one logged frame into the framebuffer. raw: palette values (screen) instead of gray.
+// Where a replay draws: framebuffer rows [row_lo, row_hi) (fb holds those rows only) and the warp's
+// copies of the render inputs.
+struct RLayout {
+    uint8_t* fb; uint8_t* vram; uint8_t* pal; uint8_t* oam; uint8_t* stage; const uint8_t* lut;
+    uint32_t* spr; uint8_t* gv;
+    int row_lo, row_hi;
+};
+__device__ __forceinline__ RLayout full_layout(uint8_t* sm) {
+    RLayout L;
+    L.fb = sm + RS_FB; L.vram = sm + RS_VRAM; L.pal = sm + RS_PAL; L.oam = sm + RS_OAM; L.stage = sm + RS_STAGE;
+    L.lut = sm + RS_LUT; L.spr = reinterpret_cast<uint32_t*>(sm + RS_SPR); L.gv = sm + RS_GV;
+    L.row_lo = 0; L.row_hi = SCREEN_H;
+    return L;
+}
+
+// Replay one logged frame into the framebuffer rows of L. raw: palette values (screen) instead of gray.
 // max_mode: combine with the frame already in the framebuffer by max (ALE-style max-pool).
 // Work split: every record is read by all lanes; a segment's dots go 8 per lane (lane L: x0 + 8L ..);
-// the line's sprite rows are fetched once per line by lanes 0..7 and broadcast with shuffles.
-__device__ void render_slot(const uint8_t* slot, uint8_t* sm, const Dev& d, bool raw, bool max_mode, int lane) {
-    uint8_t* fb = sm + RS_FB;
+// the line's sprite rows are fetched once per line by lanes 0..7 and broadcast through shared memory.
+// Records and state changes are applied in full whatever the band; only lines inside it are drawn.
+__device__ void render_slot(const uint8_t* slot, const RLayout& L, const Dev& d, bool raw, bool max_mode, int lane) {
+    uint8_t* fb = L.fb - L.row_lo * SCREEN_W;  // indexed by screen row
     RState rs;
-    rs.vram = sm + RS_VRAM; rs.pal = sm + RS_PAL; rs.oam = sm + RS_OAM; rs.chr = d.chr;
+    rs.vram = L.vram; rs.pal = L.pal; rs.oam = L.oam; rs.chr = d.chr;
     for (int i = 0; i < 4; i++) rs.nt[i] = d.nt[i];
-    uint8_t* stage = sm + RS_STAGE;
-    const uint8_t* lut = sm + RS_LUT;
+    uint8_t* stage = L.stage;
+    const uint8_t* lut = L.lut;
     {
         const uint4* hv = reinterpret_cast<const uint4*>(slot + SLOT_HDR_VRAM);
         uint4* sv = reinterpret_cast<uint4*>(rs.vram);
@@ -132,7 +150,7 @@ __device__ void render_slot(const uint8_t* slot, uint8_t* sm, const Dev& d, bool
     rs.nsl = lw[0] & 0xffu; rs.sl_lo = lw[1]; rs.sl_hi = lw[2];
     const int nrec = (int)lw[3] < d.log_cap ? (int)lw[3] : d.log_cap;
     const uint4* recs = reinterpret_cast<const uint4*>(slot + SLOT_HDR_BYTES);
-    uint8_t* gv = sm + RS_GV;
+    uint8_t* gv = L.gv;
     __syncwarp();
     {
         const uint32_t pv = rs.pal[lane];
@@ -143,7 +161,7 @@ __device__ void render_slot(const uint8_t* slot, uint8_t* sm, const Dev& d, bool
     uint32_t ver = 0;                                   // bumps on every content change (VRAM/palette/OAM)
     uint32_t lkey = 0xffffffffu, lnsl = 0, llo = 0, lhi = 0;   // cached pending-evaluation result
     uint32_t skey0 = 0xffffffffu, skey1 = 0, skey2 = 0;        // cached sprite rows of the current line
-    uint32_t* srow_s = reinterpret_cast<uint32_t*>(sm + RS_SPR);   // the line's sprite rows (list order)
+    uint32_t* srow_s = L.spr;                                   // the line's sprite rows (list order)
     uint32_t* sinfo_s = srow_s + 8;
     // records are read 32 at a time (one coalesced load, lane j holds record wb + j) and broadcast by shuffle
     int wb = -64;
@@ -161,6 +179,12 @@ __device__ void render_slot(const uint8_t* slot, uint8_t* sm, const Dev& d, bool
         if (type == REC_SEG) {
             Seg g = decode_seg(rec);
             for (;;) {  // one pass per line of the record
+                if (max_mode && first_row < 0) first_row = g.y;
+                if (g.y < L.row_lo || g.y >= L.row_hi) {         // outside the band
+                    if (g.y >= g.y1) break;
+                    seg_next_line(g);
+                    continue;
+                }
                 uint32_t nsl, lo, hi;
                 if (g.pend) {
                     uint32_t key = g.ev_y | (g.oam_addr << 8) | ((g.flags & RF_LONG) ? 0x10000u : 0u) | (ver << 17);
@@ -198,7 +222,6 @@ __device__ void render_slot(const uint8_t* slot, uint8_t* sm, const Dev& d, bool
                         __syncwarp();
                     }
                 }
-                if (max_mode && first_row < 0) first_row = g.y;
                 const bool to_stage = max_mode && g.y == first_row;
                 const int xa = g.x0 + lane * 8;
                 uint32_t outw[2];
@@ -253,17 +276,18 @@ __device__ void render_slot(const uint8_t* slot, uint8_t* sm, const Dev& d, bool
         }
         __syncwarp();
     }
-    if (max_mode && first_row >= 0) {
+    if (max_mode && first_row >= L.row_lo && first_row < L.row_hi) {
         uint8_t* row = fb + first_row * SCREEN_W;
         for (int xx = lane; xx < SCREEN_W; xx += 32) { uint8_t o = row[xx], st = stage[xx]; row[xx] = st > o ? st : o; }
     }
     __syncwarp();
 }
 
-// 84x84 area resize of the framebuffer into RS_OBS (warp-wide; lane owns columns lane, lane+32, lane+64)
-__device__ void resize_fb(uint8_t* sm, int lane) {
-    const uint8_t* fb = sm + RS_FB;
-    uint8_t* out = sm + RS_OBS;
+// Area resize of output rows [dy_lo, dy_hi) from framebuffer rows starting at screen row row_lo (fb holds
+// the rows the taps of those output rows read) into out (row dy at (dy - dy_lo) * 84). Warp-wide; lane owns
+// columns lane, lane+32, lane+64.
+__device__ void resize_band(const uint8_t* fb, int row_lo, int dy_lo, int dy_hi, uint8_t* out, int lane) {
+    fb -= row_lo * SCREEN_W;
     int32_t xs[3][6];
     float xw[3][6];
 #pragma unroll
@@ -275,7 +299,7 @@ __device__ void resize_fb(uint8_t* sm, int lane) {
             xw[q][k] = dx < OBS ? c_area.xw[k][dx] : 0.f;
         }
     }
-    for (int dy = 0; dy < OBS; dy++) {
+    for (int dy = dy_lo; dy < dy_hi; dy++) {
         float sacc[3] = {0.f, 0.f, 0.f};
         for (int m = 0; m < 6; m++) {
             float wy = c_area.yw[m][dy];
@@ -294,11 +318,13 @@ __device__ void resize_fb(uint8_t* sm, int lane) {
 #pragma unroll
         for (int q = 0; q < 3; q++) {
             int dx = lane + 32 * q;
-            if (dx < OBS) out[dy * OBS + dx] = sat_round(sacc[q]);
+            if (dx < OBS) out[(dy - dy_lo) * OBS + dx] = sat_round(sacc[q]);
         }
     }
     __syncwarp();
 }
+// the whole 84x84 frame from the full framebuffer into RS_OBS
+__device__ __forceinline__ void resize_fb(uint8_t* sm, int lane) { resize_band(sm + RS_FB, 0, 0, OBS, sm + RS_OBS, lane); }
 
 // gray LUT (or identity) into shared memory before a render phase
 __device__ __forceinline__ void load_lut(uint8_t* sm, const uint8_t* lut, int lane) {

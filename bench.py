@@ -31,7 +31,12 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 PKG_DIR = os.path.join(ROOT, "fast-mario-env_b200")
 METRIC = "agent env-steps/sec (skip 4, 84x84x4 obs)"
 UNIT = "env-steps/s"
-ALGO_BYTES_PER_STEP = 58582  # algorithmic HBM bytes per env-step (state r/w, stack r/w, scalars, outputs)
+# algorithmic HBM bytes per env-step of each kernel of the step:
+#   k_step   console state in and out (RAM+OAM+palette 2336 B and VRAM 2048 B each way, 37 scalar words each
+#            way), the frame-stack shift (3 x 7056 B read and written), actions and outputs (58 B)
+#   k_render the new 84x84 frame (7056 B) and the job word (the PPU logs it replays are the emulation
+#            kernel's intermediate output, not counted)
+ALGO_BYTES = {"k_step": 2 * (2336 + 2048) + 2 * 37 * 4 + 2 * 3 * 7056 + 58, "k_render": 7056 + 4}
 
 
 def load_package():
@@ -66,10 +71,10 @@ def read_peaks():
     return 6650.0, "fallback"
 
 
-def committed_traffic():
-    """DRAM bytes per env-step of k_step from the committed ncu summary (read + write, small-case capture
-    scaled by env count: the per-env state, stack and log traffic grow in proportion to the envs)."""
-    p = os.path.join(ROOT, "profiles", "k_step_full_config1_4096.md")
+def committed_traffic(kernel):
+    """DRAM bytes per env-step of `kernel` from its committed ncu summary (read + write of a small-case
+    capture scaled by env count: per-env state, stack and log traffic grow in proportion to the envs)."""
+    p = os.path.join(ROOT, "profiles", f"{kernel}_full_config1_4096.md")
     if os.path.exists(p):
         for line in open(p):
             if line.startswith("traffic_per_env_step_bytes"):
@@ -259,23 +264,31 @@ def main():
     env.check()
     if dist:
         dist.barrier()
+    # per step: an event before it and one between its two kernels (fme_step_marked), for the per-kernel times
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    mids = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    for e_ in starts + mids:
+        e_.record(stream)  # creates the events outside the timed region
     clocks = ClockSampler(local)
     torch.cuda.synchronize(dev)
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     ev0.record(stream)
-    for t in range(args.warmup, total):
-        env.step(acts[t])
+    for i, t in enumerate(range(args.warmup, total)):
+        starts[i].record(stream)
+        env.step(acts[t], mark=mids[i])
     ev1.record(stream)
     torch.cuda.synchronize(dev)
     clk = clocks.stop()
     ms = ev0.elapsed_time(ev1)
+    emu_ms = sum(starts[i].elapsed_time(mids[i]) for i in range(args.steps)) / args.steps
+    rend_ms = sum(mids[i].elapsed_time(starts[i + 1] if i + 1 < args.steps else ev1) for i in range(args.steps)) / args.steps
     env.check()
     if dist:
         dist.barrier()
     ms_max = shard.max_over_ranks(ms, device=dev)
     value = shard.job_throughput(world, E, args.steps, ms_max)
     ms_step = ms_max / args.steps
-    kernel_ms = ms / args.steps  # one k_step launch per step on this rank
+    kernel_ms = {"k_step": emu_ms, "k_render": rend_ms}
 
     # ---- end to end through the C ABI with host buffers (FastVecEnv.step_arrays = fme_step between a
     # pinned-host action upload and pinned-host copies of every output; final_obs rows of ended envs)
@@ -305,11 +318,12 @@ def main():
         fenv.close()
 
     peak, peak_kind = read_peaks()
-    achieved = ALGO_BYTES_PER_STEP * E / (kernel_ms / 1000.0) / 1e9
-    traffic_per_step = committed_traffic()
+    top = max(kernel_ms, key=kernel_ms.get)  # the dominant kernel of the step
+    achieved = ALGO_BYTES[top] * E / (kernel_ms[top] / 1000.0) / 1e9
+    traffic_per_step = committed_traffic(top)
     roofline = {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
                 "traffic": traffic_per_step * E if traffic_per_step else None,
-                "kernel": "k_step", "algorithmic_bytes_per_env_step": ALGO_BYTES_PER_STEP,
+                "kernel": top, "kernel_ms": kernel_ms, "algorithmic_bytes_per_env_step": ALGO_BYTES[top],
                 "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured" else "fallback 6.65 TB/s",
                 "note": "the env step is an issue-bound integer interpreter; HBM fraction is reported as required, "
                         "issue-slot figures are in profiles/"}

@@ -880,7 +880,7 @@ int fme_set_buffers(FmeEnv* v, const FmeBuffers* b) {
     return FME_OK;
 }
 
-static int launch_step_like(FmeEnv* v, const int64_t* d_actions, void* stream, bool reset) {
+static int launch_step_like(FmeEnv* v, const int64_t* d_actions, void* stream, bool reset, void* mark = nullptr) {
     if (!v) return fail(FME_E_ARG, "null env");
     if (!v->bound) return fail(FME_E_STATE, "fme_set_buffers must be called first");
     if (!reset && !d_actions) return fail(FME_E_ARG, "null actions");
@@ -898,6 +898,7 @@ static int launch_step_like(FmeEnv* v, const int64_t* d_actions, void* stream, b
     } else {
         P.jobs = v->d_jobs;
         k_step<<<groups, 32, SLAB_BYTES, s>>>(P);
+        if (mark) CK(cudaEventRecord((cudaEvent_t)mark, s));
         RenderParams R;
         R.d = d; R.jobs = v->d_jobs; R.obs = P.obs; R.fin = P.fin; R.frame_stack = P.frame_stack;
         k_render<<<(unsigned)v->n * NBANDS, 32, RB_BYTES, s>>>(R);
@@ -908,6 +909,10 @@ static int launch_step_like(FmeEnv* v, const int64_t* d_actions, void* stream, b
 
 int fme_reset(FmeEnv* v, void* stream) { return launch_step_like(v, nullptr, stream, true); }
 int fme_step(FmeEnv* v, const int64_t* d_actions, void* stream) { return launch_step_like(v, d_actions, stream, false); }
+int fme_step_marked(FmeEnv* v, const int64_t* d_actions, void* stream, void* event) {
+    if (!event) return fail(FME_E_ARG, "null event");
+    return launch_step_like(v, d_actions, stream, false, event);
+}
 
 int fme_poll_error(FmeEnv* v, uint32_t* status) {
     if (!v || !status) return fail(FME_E_ARG, "null env / status");

@@ -135,7 +135,8 @@ class CudaVecEnv:
         N.check(N.lib().fme_reset(self.h, self._stream()), "fme_reset")
         return self.obs
 
-    def step(self, actions):
+    def step(self, actions, mark=None):
+        """mark: optional torch.cuda.Event, recorded between the emulation and the render kernel."""
         torch = _torch()
         if not isinstance(actions, torch.Tensor):
             actions = torch.as_tensor(np.asarray(actions), dtype=torch.int64)
@@ -145,7 +146,11 @@ class CudaVecEnv:
             raise ValueError(f"expected {self.n} actions, got {actions.numel()}")
         if actions.data_ptr() != self.actions.data_ptr():
             self.actions.copy_(actions.view(-1))
-        N.check(N.lib().fme_step(self.h, N.ptr(self.actions), self._stream()), "fme_step")
+        if mark is None:
+            N.check(N.lib().fme_step(self.h, N.ptr(self.actions), self._stream()), "fme_step")
+        else:
+            N.check(N.lib().fme_step_marked(self.h, N.ptr(self.actions), self._stream(), ctypes.c_void_p(mark.cuda_event)),
+                    "fme_step_marked")
         return self.obs, self.rew, self.term, self.trunc, self.info
 
     def ram(self):

@@ -97,6 +97,10 @@ int fme_reset(FmeEnv* env, void* stream);
  * (cuda/vec_env.py:367-373): sticky actions, frame skip, max-pool, reward/done/info, busy-state skipping,
  * time limit, frame stack, final_obs and auto-reset. Async; enqueues only. */
 int fme_step(FmeEnv* env, const int64_t* d_actions, void* stream);
+/* fme_step that also records `event` (a cudaEvent_t as void*, created by the caller) on the stream between
+ * the emulation kernel and the render kernel, so the two can be timed apart. No counterpart in the
+ * reference (a profiling hook; the step itself is identical). */
+int fme_step_marked(FmeEnv* env, const int64_t* d_actions, void* stream, void* event);
 
 /* OR of the device status bits of all envs since create (call after synchronising). */
 int fme_poll_error(FmeEnv* env, uint32_t* status);

@@ -59,7 +59,7 @@ __global__ void __launch_bounds__(32) k_boot(BootParams P) {
     // Boot protocol of SuperMarioBrosEnv (fastmario.cpp:422-445), one frame per call of the state machine:
     // phase 0 fa(8), 1 fa(0), then loop A {2: fa(8); write level; 3: fa(0); $7A0=0} while time==0,
     // then loop B {4: fa(8), 5: fa(0)} while time >= tl.
-    const Fast fst{c.ram, d.prg};
+    const Fast fst{c.ram, d.prg, d.uop};
     Hot h;
     hot_in(h, c, fst);
     while (__any_sync(FULL, running)) {
@@ -162,7 +162,7 @@ __global__ void __launch_bounds__(32) k_step(StepParams P) {
     bool running = active;
     if (active) ag.start(c, ev, cfg, act, d.logs + slot_off(e, 0, cap), d.logs + slot_off(e, 1, cap));
     // one emulated instruction per lane per iteration; the vote keeps the warp converged at the loop head
-    const Fast fst{c.ram, d.prg};
+    const Fast fst{c.ram, d.prg, d.uop};
     Hot h;
     hot_in(h, c, fst);
     while (__any_sync(FULL, running)) {
@@ -448,7 +448,7 @@ __global__ void __launch_bounds__(32) k_raw(RawParams P) {
     uint8_t* slot = d.logs + slot_off(e, 0, d.log_cap);
     bool running = active;
     if (active) begin_frame(c, slot, P.buttons[e], d.log_cap);
-    const Fast fst{c.ram, d.prg};
+    const Fast fst{c.ram, d.prg, d.uop};
     Hot h;
     hot_in(h, c, fst);
     while (__any_sync(FULL, running)) {
@@ -631,11 +631,25 @@ struct DevBufs {  // one set of per-env state buffers
     }
 };
 
+// The PRG image and its micro-op table share one allocation: 32 KB of PRG, then 2 words per PRG address.
+constexpr size_t PRG_UOP_OFF = 0x8000;
+constexpr size_t PRG_ALLOC = PRG_UOP_OFF + (size_t)UOP_WORDS * 4;
+cudaError_t upload_prg(uint8_t* d_prg, const std::vector<uint8_t>& prg) {
+    uint32_t dt[256];
+    build_dtab(dt);
+    std::vector<uint32_t> uops(UOP_WORDS);
+    build_uops(prg.data(), dt, uops.data());
+    cudaError_t e = cudaMemcpy(d_prg, prg.data(), 0x8000, cudaMemcpyHostToDevice);
+    if (e == cudaSuccess) e = cudaMemcpy(d_prg + PRG_UOP_OFF, uops.data(), (size_t)UOP_WORDS * 4, cudaMemcpyHostToDevice);
+    return e;
+}
+
 Dev make_dev(const DevBufs& b, const uint8_t* prg, const uint8_t* chr, const uint32_t nt[4], const uint8_t* lut,
              uint32_t* err) {
     Dev d;
     d.n = b.n; d.n_pad = b.n_pad; d.slab = b.slab; d.vram = b.vram; d.scal = b.scal; d.logs = b.logs;
     d.log_cap = b.log_cap; d.prg = prg; d.chr = chr;
+    d.uop = reinterpret_cast<const uint32_t*>(prg + PRG_UOP_OFF);
     for (int i = 0; i < 4; i++) d.nt[i] = nt[i];
     d.lut = lut; d.err = err;
     return d;
@@ -748,12 +762,12 @@ static int create_impl(const FmeConfig* cfg, const uint8_t* rom, int64_t rom_len
     const int nl = (int)(uniq.size() / 3);
     v->nl = nl;
     const int nk = C.noop_max + 1;
-    CK(cudaMalloc(&v->d_prg, 0x8000));
+    CK(cudaMalloc(&v->d_prg, PRG_ALLOC));
     CK(cudaMalloc(&v->d_chr, 0x2000));
     CK(cudaMalloc(&v->d_lut, 256));
     CK(cudaMalloc(&v->d_err, 4));
     CK(cudaMalloc(&v->d_jobs, (size_t)(C.n_envs + 31) / 32 * 32 * 4));
-    CK(cudaMemcpy(v->d_prg, prg.data(), 0x8000, cudaMemcpyHostToDevice));
+    CK(upload_prg(v->d_prg, prg));
     CK(cudaMemcpy(v->d_chr, chr.data(), 0x2000, cudaMemcpyHostToDevice));
     CK(cudaMemcpy(v->d_lut, gray_lut, 256, cudaMemcpyHostToDevice));
     CK(cudaMemset(v->d_err, 0, 4));
@@ -988,13 +1002,13 @@ int fme_raw_create(const uint8_t* rom, int64_t rom_len, int32_t n, int32_t devic
     if (rc) return bail(rc);
     uint8_t ident[256];
     for (int i = 0; i < 256; i++) ident[i] = (uint8_t)i;
-    if (cudaMalloc(&r->d_prg, 0x8000) || cudaMalloc(&r->d_chr, 0x2000) || cudaMalloc(&r->d_lut, 256) ||
+    if (cudaMalloc(&r->d_prg, PRG_ALLOC) || cudaMalloc(&r->d_chr, 0x2000) || cudaMalloc(&r->d_lut, 256) ||
         cudaMalloc(&r->d_err, 4) || cudaMalloc(&r->d_screens, (size_t)n * SCREEN_W * SCREEN_H) ||
         cudaMalloc(&r->d_bk_slab, (size_t)(r->st.n_pad / 32) * SLAB_BYTES) ||
         cudaMalloc(&r->d_bk_vram, (size_t)r->st.n_pad * VRAM_BYTES) ||
         cudaMalloc(&r->d_bk_scal, (size_t)S_WORDS * r->st.n_pad * 4))
         return bail(fail(FME_E_CUDA, "cudaMalloc failed"));
-    cudaMemcpy(r->d_prg, prg.data(), 0x8000, cudaMemcpyHostToDevice);
+    if (upload_prg(r->d_prg, prg) != cudaSuccess) return bail(fail(FME_E_CUDA, "PRG upload failed"));
     cudaMemcpy(r->d_chr, chr.data(), 0x2000, cudaMemcpyHostToDevice);
     cudaMemcpy(r->d_lut, ident, 256, cudaMemcpyHostToDevice);
     cudaMemset(r->d_err, 0, 4);

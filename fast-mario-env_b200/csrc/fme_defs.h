@@ -69,6 +69,19 @@ FME_HD uint32_t d_op(uint32_t d) { return (d >> 8) & 31u; }
 FME_HD uint32_t d_pen(uint32_t d) { return (d >> 13) & 1u; }
 FME_HD uint32_t d_cycles(uint32_t d) { return (d >> 16) & 255u; }
 
+// ---------------------------------------------------------------- per-PC micro-op (fast path)
+// word 0: handler | opcode<<8 | op<<16 | page-penalty<<21 | length<<22 | idle-loop<<24
+// word 1: operand (immediate or ROM value, static address, pointer byte, branch target) | cycles<<16 | extra<<24
+enum Hid : uint32_t {
+    H_SLOW = 0,   // the exact path (I/O operands, code at $FFFE-$FFFF, unusual forms)
+    H_RD_IMM, H_RD_ZP, H_RD_ZPX, H_RD_ZPY, H_RD_ABS, H_RD_ABSX, H_RD_ABSY, H_RD_INDX, H_RD_INDY,
+    H_ST_ZP, H_ST_ZPX, H_ST_ZPY, H_ST_ABS, H_ST_ABSX, H_ST_ABSY, H_ST_INDX, H_ST_INDY, H_NOPW,
+    H_RMW_ZP, H_RMW_ZPX, H_RMW_ABS, H_RMW_ABSX,
+    H_ACC, H_BRANCH, H_IMPL, H_BAD, H_BAD_ABSX,
+};
+constexpr uint32_t UOP_IDLE = 1u << 24;
+constexpr int UOP_WORDS = 2 * 0x8000;
+
 // ---------------------------------------------------------------- log records (16 B each)
 enum RecType : uint32_t { REC_SEG = 0, REC_VRAM = 1, REC_PAL = 2, REC_OAM = 3, REC_DMA = 4, REC_LIST = 5, REC_VSNAP = 6 };
 // VRAM writes logged one by one between two segments; past this many the next segment is preceded by a

@@ -3,10 +3,11 @@
 // The full console (`Core`, fme_core.h) is the exact model; its I/O, PPU and NMI code is large and rarely
 // needed per instruction. Keeping the whole object in registers is not possible once that code is out of
 // line, so the loop works on `Hot`: the 6502 registers, the frame clock and the NMI threshold, held by value
-// (its address is never taken, so it stays in registers). Every instruction whose memory accesses are RAM or
-// PRG only runs here with the semantics of Core::execute_op (nes_core.hpp:645-1163); an instruction that
-// would touch $2000-$7FFF (PPU registers, joypads, OAM DMA), or code outside PRG, is handed to the exact
-// Core path with Hot written back first. Nothing here has side effects before that decision.
+// (its address is never taken, so it stays in registers). Instructions are executed from per-PC micro-ops
+// built once per ROM (fme_tables.h build_uops): every instruction whose memory accesses are RAM or PRG only
+// runs here with the semantics of Core::execute_op (nes_core.hpp:645-1163); an instruction that would touch
+// $2000-$7FFF (PPU registers, joypads, OAM DMA), or code outside PRG, is handed to the exact Core path with
+// Hot written back first. Nothing here has side effects before that decision.
 #pragma once
 #include "fme_core.h"
 
@@ -16,7 +17,7 @@ struct Hot {
     uint32_t pc, a, x, y, sp, p;
     int32_t exec_at, thresh;
     uint32_t zero_skip, bad;
-    uint32_t op, b1, b2;  // bytes at pc, pc+1, pc+2 as rd_prg_fast reads them (0xff outside PRG)
+    uint32_t ux, uy;  // micro-op of the instruction at pc (fme_defs.h); zero outside PRG
 };
 
 // Exact slow paths (the Core methods), out of line so the hot loop stays small.
@@ -33,14 +34,23 @@ FME_NI int32_t slow_execute(Core& c, int32_t J, uint32_t opc) {
 struct Fast {
     uint8_t* ram;            // lane base of the RAM slab
     const uint8_t* prg;
+    const uint32_t* uop;     // per-PC micro-ops, 2 words per address $8000-$FFFF
 
     FME_HD uint32_t P(uint32_t a) const { return FME_LDG(prg + (a & 0x7fffu)); }
-    FME_HD uint32_t pf(uint32_t a) const { a &= 0xffffu; return a >= 0x8000u ? P(a) : 0xffu; }
     FME_HD uint32_t R(uint32_t a) const { return ram[il(a & 0x7ffu)]; }
     FME_HD void W(uint32_t a, uint32_t v) const { ram[il(a & 0x7ffu)] = (uint8_t)v; }
     // side-effect-free read of an address outside $2000-$7FFF
     FME_HD uint32_t M(uint32_t a) const { return a >= 0x8000u ? P(a) : R(a); }
     FME_HD static bool io(uint32_t a) { return a >= 0x2000u && a < 0x8000u; }
+    FME_HD uint2 U(uint32_t pc) const {
+#if defined(__CUDA_ARCH__)
+        return __ldg(reinterpret_cast<const uint2*>(uop) + (pc - 0x8000u));
+#else
+        uint2 u;
+        u.x = uop[2 * (pc - 0x8000u)]; u.y = uop[2 * (pc - 0x8000u) + 1];
+        return u;
+#endif
+    }
 
     FME_HD static void zn(Hot& h, uint32_t v) {
         v &= 0xffu;
@@ -48,105 +58,87 @@ struct Fast {
     }
     FME_HD static void setf(Hot& h, uint32_t f, bool on) { h.p = on ? (h.p | f) : (h.p & ~f); }
 
-    // Execute the instruction with opcode `opc` at h.pc (pc in $8000-$FFFD). Returns the skip-cycle count, or
-    // -1 if the instruction needs the exact path (nothing was changed then).
-    FME_HD int32_t exec(Hot& h, uint32_t opc) const {
-        const uint32_t d = FME_DTAB(opc);
-        const uint32_t kind = d_kind(d), op = d_op(d);
-        const uint32_t b1 = h.b1, b2 = h.b2;  // pc <= $FFFD: both come from PRG
-        int32_t skip = 0;
-        uint32_t npc = (h.pc + 1) & 0xffffu;
-        switch (kind) {
-            case K_READ: case K_STORE: case K_RMW: {
-                const uint32_t mode = d_mode(d);
-                uint32_t loc = 0, base = 0;
-                switch (mode) {
-                    case M_IMM: loc = npc; npc += 1; break;
-                    case M_ZP: loc = b1; npc += 1; break;
-                    case M_ZPX: loc = (b1 + h.x) & 0xffu; npc += 1; break;
-                    case M_ZPY: loc = (b1 + h.y) & 0xffu; npc += 1; break;
-                    case M_ABS: loc = b1 | (b2 << 8); npc += 2; break;
-                    case M_ABSX: base = b1 | (b2 << 8); loc = (base + h.x) & 0xffffu; npc += 2; break;
-                    case M_ABSY: base = b1 | (b2 << 8); loc = (base + h.y) & 0xffffu; npc += 2; break;
-                    case M_INDX: { uint32_t za = (h.x + b1) & 0xffu; loc = R(za) | (R((za + 1) & 0xffu) << 8); npc += 1; break; }
-                    default: {  // M_INDY
-                        base = R(b1) | (R((b1 + 1) & 0xffu) << 8);
-                        loc = (base + h.y) & 0xffffu; npc += 1; break;
-                    }
-                }
-                if (io(loc)) return -1;
-                if (d_pen(d) && (mode == M_ABSX || mode == M_ABSY || mode == M_INDY) && ((base ^ loc) & 0xff00u)) skip += 1;
-                if (kind == K_READ) {
-                    const uint32_t m = M(loc);
-                    switch (op) {
-                        case R_ORA: h.a |= m; zn(h, h.a); break;
-                        case R_AND: h.a &= m; zn(h, h.a); break;
-                        case R_EOR: h.a ^= m; zn(h, h.a); break;
-                        case R_ADC: {
-                            uint32_t sum = h.a + m + ((h.p & F_C) ? 1u : 0u);
-                            setf(h, F_C, sum & 0x100u);
-                            setf(h, F_V, (h.a ^ sum) & (m ^ sum) & 0x80u);
-                            h.a = sum & 0xffu; zn(h, h.a);
-                            break;
-                        }
-                        case R_LDA: h.a = m; zn(h, h.a); break;
-                        case R_CMP: { uint32_t t = (h.a - m) & 0xffffu; setf(h, F_C, !(t & 0x100u)); zn(h, t); break; }
-                        case R_SBC: {
-                            uint32_t t = (h.a - m - ((h.p & F_C) ? 0u : 1u)) & 0xffffu;
-                            setf(h, F_C, !(t & 0x100u));
-                            setf(h, F_V, (h.a ^ t) & (~m ^ t) & 0x80u);
-                            h.a = t & 0xffu; zn(h, t);
-                            break;
-                        }
-                        case R_BIT: setf(h, F_Z, !(h.a & m)); setf(h, F_V, m & 0x40u); setf(h, F_N, m & 0x80u); break;
-                        case R_LDX: h.x = m; zn(h, h.x); break;
-                        case R_LDY: h.y = m; zn(h, h.y); break;
-                        case R_CPX: { uint32_t t = (h.x - m) & 0xffffu; setf(h, F_C, !(t & 0x100u)); zn(h, t); break; }
-                        default:    { uint32_t t = (h.y - m) & 0xffffu; setf(h, F_C, !(t & 0x100u)); zn(h, t); break; }
-                    }
-                } else if (kind == K_STORE) {
-                    if (loc < 0x2000u) W(loc, op == W_STA ? h.a : op == W_STX ? h.x : h.y);  // PRG writes are ignored
-                } else {
-                    uint32_t m = M(loc);
-                    const uint32_t c = (h.p & F_C) ? 1u : 0u;
-                    switch (op) {
-                        case X_ASL: setf(h, F_C, m & 0x80u); m = (m << 1) & 0xffu; break;
-                        case X_ROL: setf(h, F_C, m & 0x80u); m = ((m << 1) | c) & 0xffu; break;
-                        case X_LSR: setf(h, F_C, m & 1u); m >>= 1; break;
-                        case X_ROR: setf(h, F_C, m & 1u); m = (m >> 1) | (c << 7); break;
-                        case X_DEC: m = (m - 1) & 0xffu; break;
-                        default: m = (m + 1) & 0xffu; break;
-                    }
-                    zn(h, m);
-                    if (loc < 0x2000u) W(loc, m);
-                }
+    FME_HD static void alu_read(Hot& h, uint32_t op, uint32_t m) {
+        switch (op) {
+            case R_ORA: h.a |= m; zn(h, h.a); break;
+            case R_AND: h.a &= m; zn(h, h.a); break;
+            case R_EOR: h.a ^= m; zn(h, h.a); break;
+            case R_ADC: {
+                uint32_t sum = h.a + m + ((h.p & F_C) ? 1u : 0u);
+                setf(h, F_C, sum & 0x100u);
+                setf(h, F_V, (h.a ^ sum) & (m ^ sum) & 0x80u);
+                h.a = sum & 0xffu; zn(h, h.a);
                 break;
             }
-            case K_BRANCH: {
-                const uint32_t f = (h.p >> (op & 7u)) & 1u;
-                npc = (npc + 1) & 0xffffu;
-                if (f == ((op >> 3) & 1u)) {
-                    skip += 1;
-                    const uint32_t t = (uint32_t)((int32_t)npc + (int32_t)(int8_t)(uint8_t)b1) & 0xffffu;
-                    if ((t ^ npc) & 0xff00u) skip += 2;
-                    npc = t;
-                }
+            case R_LDA: h.a = m; zn(h, h.a); break;
+            case R_CMP: { uint32_t t = (h.a - m) & 0xffffu; setf(h, F_C, !(t & 0x100u)); zn(h, t); break; }
+            case R_SBC: {
+                uint32_t t = (h.a - m - ((h.p & F_C) ? 0u : 1u)) & 0xffffu;
+                setf(h, F_C, !(t & 0x100u));
+                setf(h, F_V, (h.a ^ t) & (~m ^ t) & 0x80u);
+                h.a = t & 0xffu; zn(h, t);
                 break;
             }
-            case K_ACC: {
-                uint32_t m = h.a;
-                const uint32_t c = (h.p & F_C) ? 1u : 0u;
-                switch (op) {
-                    case X_ASL: setf(h, F_C, m & 0x80u); m = (m << 1) & 0xffu; break;
-                    case X_ROL: setf(h, F_C, m & 0x80u); m = ((m << 1) | c) & 0xffu; break;
-                    case X_LSR: setf(h, F_C, m & 1u); m >>= 1; break;
-                    default: setf(h, F_C, m & 1u); m = (m >> 1) | (c << 7); break;
-                }
-                zn(h, m);
-                h.a = m;
+            case R_BIT: setf(h, F_Z, !(h.a & m)); setf(h, F_V, m & 0x40u); setf(h, F_N, m & 0x80u); break;
+            case R_LDX: h.x = m; zn(h, h.x); break;
+            case R_LDY: h.y = m; zn(h, h.y); break;
+            case R_CPX: { uint32_t t = (h.x - m) & 0xffffu; setf(h, F_C, !(t & 0x100u)); zn(h, t); break; }
+            default:    { uint32_t t = (h.y - m) & 0xffffu; setf(h, F_C, !(t & 0x100u)); zn(h, t); break; }
+        }
+    }
+    FME_HD static uint32_t alu_rmw(Hot& h, uint32_t op, uint32_t m) {
+        const uint32_t c = (h.p & F_C) ? 1u : 0u;
+        switch (op) {
+            case X_ASL: setf(h, F_C, m & 0x80u); m = (m << 1) & 0xffu; break;
+            case X_ROL: setf(h, F_C, m & 0x80u); m = ((m << 1) | c) & 0xffu; break;
+            case X_LSR: setf(h, F_C, m & 1u); m >>= 1; break;
+            case X_ROR: setf(h, F_C, m & 1u); m = (m >> 1) | (c << 7); break;
+            case X_DEC: m = (m - 1) & 0xffu; break;
+            default: m = (m + 1) & 0xffu; break;
+        }
+        zn(h, m);
+        return m;
+    }
+
+    // Execute the instruction at h.pc from its micro-op (h.ux, h.uy; not H_SLOW) with the semantics of
+    // Core::execute_op. Returns the skip-cycle count, or -1 if a computed address is an I/O address and the
+    // exact path must run it instead (nothing was changed then).
+    FME_HD int32_t exec(Hot& h) const {
+        const uint32_t hid = h.ux & 0xffu, op = (h.ux >> 16) & 31u, pen = (h.ux >> 21) & 1u;
+        const uint32_t w = h.uy & 0xffffu;
+        int32_t skip = (int32_t)((h.uy >> 16) & 0xffu);
+        uint32_t npc = (h.pc + ((h.ux >> 22) & 3u)) & 0xffffu;
+        uint32_t loc = 0, base = 0;
+        int cls = 3;  // 0 read m, 1 store to loc, 2 read-modify-write loc, 3 done
+        uint32_t m = 0;
+        switch (hid) {
+            case H_RD_IMM: m = w; cls = 0; break;
+            case H_RD_ZP: m = R(w); cls = 0; break;
+            case H_RD_ZPX: m = R((w + h.x) & 0xffu); cls = 0; break;
+            case H_RD_ZPY: m = R((w + h.y) & 0xffu); cls = 0; break;
+            case H_RD_ABS: m = R(w); cls = 0; break;
+            case H_RD_ABSX: base = w; loc = (w + h.x) & 0xffffu; cls = 4; break;
+            case H_RD_ABSY: base = w; loc = (w + h.y) & 0xffffu; cls = 4; break;
+            case H_RD_INDX: { const uint32_t za = (h.x + w) & 0xffu; loc = R(za) | (R((za + 1) & 0xffu) << 8); cls = 4; break; }
+            case H_RD_INDY: base = R(w) | (R((w + 1) & 0xffu) << 8); loc = (base + h.y) & 0xffffu; cls = 4; break;
+            case H_ST_ZP: loc = w; cls = 1; break;
+            case H_ST_ZPX: loc = (w + h.x) & 0xffu; cls = 1; break;
+            case H_ST_ZPY: loc = (w + h.y) & 0xffu; cls = 1; break;
+            case H_ST_ABS: loc = w; cls = 1; break;
+            case H_ST_ABSX: base = w; loc = (w + h.x) & 0xffffu; cls = 5; break;
+            case H_ST_ABSY: base = w; loc = (w + h.y) & 0xffffu; cls = 5; break;
+            case H_ST_INDX: { const uint32_t za = (h.x + w) & 0xffu; loc = R(za) | (R((za + 1) & 0xffu) << 8); cls = 5; break; }
+            case H_ST_INDY: base = R(w) | (R((w + 1) & 0xffu) << 8); loc = (base + h.y) & 0xffffu; cls = 5; break;
+            case H_NOPW: break;
+            case H_RMW_ZP: loc = w; cls = 2; break;
+            case H_RMW_ZPX: loc = (w + h.x) & 0xffu; cls = 2; break;
+            case H_RMW_ABS: loc = w; cls = 2; break;
+            case H_RMW_ABSX: base = w; loc = (w + h.x) & 0xffffu; cls = 6; break;
+            case H_ACC: h.a = alu_rmw(h, op, h.a); break;
+            case H_BRANCH:
+                if (((h.p >> (op & 7u)) & 1u) == ((op >> 3) & 1u)) { skip += (int32_t)(h.uy >> 24); npc = w; }
                 break;
-            }
-            case K_IMPL: {
+            case H_IMPL:
                 switch (op) {
                     case I_BRK: {
                         uint32_t r = npc + 1;  // BRK skips its padding byte
@@ -164,7 +156,7 @@ struct Fast {
                         uint32_t r = (npc + 1) & 0x1ffffu;
                         W(0x100u | h.sp, (r >> 8) & 0xffu); h.sp = (h.sp - 1) & 0xffu;
                         W(0x100u | h.sp, r & 0xffu); h.sp = (h.sp - 1) & 0xffu;
-                        npc = b1 | (b2 << 8);
+                        npc = w;
                         break;
                     }
                     case I_PLP: h.sp = (h.sp + 1) & 0xffu; h.p = R(0x100u | h.sp); break;
@@ -176,7 +168,7 @@ struct Fast {
                         break;
                     }
                     case I_PHA: W(0x100u | h.sp, h.a); h.sp = (h.sp - 1) & 0xffu; break;
-                    case I_JMP: npc = b1 | (b2 << 8); break;
+                    case I_JMP: npc = w; break;
                     case I_CLI: setf(h, F_I, false); break;
                     case I_RTS: {
                         h.sp = (h.sp + 1) & 0xffu; uint32_t lo = R(0x100u | h.sp);
@@ -184,11 +176,9 @@ struct Fast {
                         break;
                     }
                     case I_PLA: h.sp = (h.sp + 1) & 0xffu; h.a = R(0x100u | h.sp); zn(h, h.a); break;
-                    case I_JMPI: {
-                        const uint32_t loc = b1 | (b2 << 8);
-                        const uint32_t hiad = (loc & 0xff00u) | ((loc + 1) & 0xffu);
-                        if (io(loc) || io(hiad)) return -1;
-                        npc = M(loc) | (M(hiad) << 8);
+                    case I_JMPI: {  // the builder routed I/O pointer addresses to the exact path
+                        const uint32_t hiad = (w & 0xff00u) | ((w + 1) & 0xffu);
+                        npc = M(w) | (M(hiad) << 8);
                         break;
                     }
                     case I_SEI: setf(h, F_I, true); break;
@@ -208,31 +198,38 @@ struct Fast {
                     default: setf(h, F_D, true); break;  // SED
                 }
                 break;
-            }
-            case K_BAD_ZP: h.bad++; npc += 1; break;
-            case K_BAD_ABS: h.bad++; npc += 2; break;
-            case K_BAD_ABSX: {
-                const uint32_t b = b1 | (b2 << 8);
-                if (((b + h.x) ^ b) & 0xff00u) skip += 1;
-                h.bad++; npc += 2;
+            case H_BAD_ABSX:
+                if (((w + h.x) ^ w) & 0xff00u) skip += 1;
+                h.bad++;
                 break;
-            }
-            default: h.bad++; break;
+            default: h.bad++; break;  // H_BAD
         }
-        h.pc = npc & 0xffffu;
-        if (kind >= K_IMPL) skip += (int32_t)d_cycles(d);
+        if (cls >= 4) {  // computed address: I/O goes to the exact path, then the page-cross penalty
+            if (io(loc)) return -1;
+            if (pen && ((base ^ loc) & 0xff00u)) skip += 1;
+            cls -= 4;
+            if (cls == 0) m = M(loc);
+        }
+        if (cls == 0) {
+            alu_read(h, op, m);
+        } else if (cls == 1) {
+            if (loc < 0x2000u) W(loc, op == W_STA ? h.a : op == W_STX ? h.x : h.y);  // ROM writes are ignored
+        } else if (cls == 2) {
+            const uint32_t r = alu_rmw(h, op, M(loc));
+            if (loc < 0x2000u) W(loc, r);
+        }
+        h.pc = npc;
         return skip;
     }
 };
 
-// Prefetch of the instruction bytes at the new pc: the next iteration's idle test, decode and the
-// scheduler's vote all read them, so the loads overlap the loop head instead of following it.
+// Micro-op of the instruction at the new pc: the next iteration's scheduler vote, idle test and decode
+// read it, so the load overlaps the loop head instead of following it.
 FME_HD void fetch(Hot& h, const Fast& f) {
-    h.op = h.pc >= 0x8000u ? f.P(h.pc) : 0xffu;
-    h.b1 = f.pf(h.pc + 1);
-    h.b2 = f.pf(h.pc + 2);
+    if (h.pc >= 0x8000u) { const uint2 u = f.U(h.pc); h.ux = u.x; h.uy = u.y; }
+    else { h.ux = 0u; h.uy = 0u; }
 }
-FME_HD bool idle_loop(const Hot& h) { return h.op == 0x4Cu && (h.b1 | (h.b2 << 8)) == h.pc; }  // JMP to itself
+FME_HD bool idle_loop(const Hot& h) { return (h.ux & UOP_IDLE) != 0u; }  // `JMP *` (rd_prg_fast bytes)
 FME_HD void hot_out(const Hot& h, Core& c) {
     c.pc = h.pc; c.a = h.a; c.x = h.x; c.y = h.y; c.sp = h.sp; c.p = h.p;
     c.exec_at = h.exec_at; c.nmi_thresh = h.thresh; c.zero_skip = h.zero_skip != 0; c.bad_ops = h.bad;
@@ -267,10 +264,9 @@ FME_HD bool hot_step(Hot& h, Core& c, const Fast& f) {
             return true;
         }
     }
-    const bool in_prg = h.pc >= 0x8000u && h.pc <= 0xfffdu;  // operand bytes then come from PRG too
-    const uint32_t opc = in_prg ? h.op : 0x100u;
-    int32_t S = in_prg ? f.exec(h, opc) : -1;
+    int32_t S = (h.ux & 0xffu) != H_SLOW ? f.exec(h) : -1;
     if (S < 0) {
+        const uint32_t opc = h.pc >= 0x8000u ? (h.ux >> 8) & 0xffu : 0x100u;
         hot_out(h, c);
         S = slow_execute(c, J, opc);
         hot_in(h, c, f);

@@ -32,6 +32,7 @@ struct Dev {
     uint8_t* logs;      // n_pad x 2 slots
     int log_cap;
     const uint8_t* prg;
+    const uint32_t* uop; // per-PC micro-ops (fme_tables.h build_uops), stored right after the 32 KB PRG
     const uint8_t* chr;
     uint32_t nt[4];
     const uint8_t* lut; // 256 gray LUT (global)

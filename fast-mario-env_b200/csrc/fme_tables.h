@@ -132,6 +132,96 @@ inline std::vector<Tap> area_taps(int ssize, int dsize) {
     }
     return out;
 }
+// Per-PC micro-ops of the fast path (fme_fast.h): the decode of the instruction at every PRG address, with
+// what the ROM fixes already resolved (static addresses, immediate and ROM operands, branch targets and
+// their page-cross cost). Addresses whose instruction needs the exact path get H_SLOW.
+inline bool io_addr(uint32_t a) { return a >= 0x2000u && a < 0x8000u; }
+inline void build_uops(const uint8_t* prg, const uint32_t* dtab, uint32_t* out /* 2 x 32768 words */) {
+    auto P = [&](uint32_t a) -> uint32_t { return prg[a & 0x7fffu]; };
+    auto pf = [&](uint32_t a) -> uint32_t { a &= 0xffffu; return a >= 0x8000u ? P(a) : 0xffu; };
+    for (uint32_t a = 0x8000u; a <= 0xffffu; a++) {
+        const uint32_t opc = P(a), d = dtab[opc];
+        const uint32_t kind = d_kind(d), mode = d_mode(d), op = d_op(d), pen = d_pen(d);
+        const uint32_t b1 = pf(a + 1), b2 = pf(a + 2), w16 = b1 | (b2 << 8);
+        const uint32_t cyc = kind >= K_IMPL ? d_cycles(d) : 0u;
+        const bool idle = opc == 0x4Cu && w16 == a;  // `JMP *` with rd_prg_fast operand bytes
+        uint32_t hid = H_SLOW, len = 1, w = 0, extra = 0;
+        if (a <= 0xfffdu) {  // operand bytes inside PRG
+            const uint32_t mlen = (mode == M_ABS || mode == M_ABSX || mode == M_ABSY) ? 3u : (mode == M_NONE ? 1u : 2u);
+            switch (kind) {
+                case K_READ:
+                    len = mlen;
+                    switch (mode) {
+                        case M_IMM: hid = H_RD_IMM; w = b1; break;
+                        case M_ZP: hid = H_RD_ZP; w = b1; break;
+                        case M_ZPX: hid = H_RD_ZPX; w = b1; break;
+                        case M_ZPY: hid = H_RD_ZPY; w = b1; break;
+                        case M_ABS:
+                            if (w16 < 0x2000u) { hid = H_RD_ABS; w = w16; }
+                            else if (w16 >= 0x8000u) { hid = H_RD_IMM; w = P(w16); }  // ROM operand
+                            break;
+                        case M_ABSX: hid = H_RD_ABSX; w = w16; break;
+                        case M_ABSY: hid = H_RD_ABSY; w = w16; break;
+                        case M_INDX: hid = H_RD_INDX; w = b1; break;
+                        case M_INDY: hid = H_RD_INDY; w = b1; break;
+                        default: break;
+                    }
+                    break;
+                case K_STORE:
+                    len = mlen;
+                    switch (mode) {
+                        case M_IMM: hid = H_NOPW; break;                          // writes into ROM: no effect
+                        case M_ZP: hid = H_ST_ZP; w = b1; break;
+                        case M_ZPX: hid = H_ST_ZPX; w = b1; break;
+                        case M_ZPY: hid = H_ST_ZPY; w = b1; break;
+                        case M_ABS:
+                            if (w16 < 0x2000u) { hid = H_ST_ABS; w = w16; }
+                            else if (w16 >= 0x8000u) hid = H_NOPW;
+                            break;
+                        case M_ABSX: hid = H_ST_ABSX; w = w16; break;
+                        case M_ABSY: hid = H_ST_ABSY; w = w16; break;
+                        case M_INDX: hid = H_ST_INDX; w = b1; break;
+                        case M_INDY: hid = H_ST_INDY; w = b1; break;
+                        default: break;
+                    }
+                    break;
+                case K_RMW:
+                    len = mlen;
+                    switch (mode) {
+                        case M_ZP: hid = H_RMW_ZP; w = b1; break;
+                        case M_ZPX: hid = H_RMW_ZPX; w = b1; break;
+                        case M_ABS: if (w16 < 0x2000u) { hid = H_RMW_ABS; w = w16; } break;
+                        case M_ABSX: hid = H_RMW_ABSX; w = w16; break;
+                        default: break;  // immediate / ROM targets: exact path
+                    }
+                    break;
+                case K_ACC: hid = H_ACC; break;
+                case K_BRANCH: {
+                    len = 2;
+                    const uint32_t npc = (a + 2u) & 0xffffu;
+                    const uint32_t t = (uint32_t)((int32_t)npc + (int32_t)(int8_t)(uint8_t)b1) & 0xffffu;
+                    hid = H_BRANCH; w = t; extra = 1u + (((t ^ npc) & 0xff00u) ? 2u : 0u);
+                    break;
+                }
+                case K_IMPL:
+                    hid = H_IMPL; w = w16;
+                    if (op == I_JMPI) {
+                        const uint32_t hiad = (w16 & 0xff00u) | ((w16 + 1u) & 0xffu);
+                        if (io_addr(w16) || io_addr(hiad)) hid = H_SLOW;
+                    }
+                    break;
+                case K_BAD_ZP: hid = H_BAD; len = 2; break;
+                case K_BAD_ABS: hid = H_BAD; len = 3; break;
+                case K_BAD_ABSX: hid = H_BAD_ABSX; len = 3; w = w16; break;
+                default: hid = H_BAD; len = 1; break;
+            }
+        }
+        if (hid == H_SLOW) { len = 0; w = w16; }  // operand kept for diagnostics only
+        out[2 * (a - 0x8000u)] = hid | (opc << 8) | (op << 16) | (pen << 21) | (len << 22) | ((idle ? 1u : 0u) << 24);
+        out[2 * (a - 0x8000u) + 1] = (w & 0xffffu) | (cyc << 16) | (extra << 24);
+    }
+}
+
 inline bool build_area(AreaTabs& T) {
     memset(&T, 0, sizeof(T));
     int cnt[OBS];

@@ -54,6 +54,11 @@ __global__ void __launch_bounds__(32) k_boot(BootParams P) {
         c.bad_ops = 0;
         c.power_on();
         begin_frame(c, slot, 8, d.log_cap);
+    } else {
+        uint32_t zw[S_CONSOLE_WORDS];
+        for (int k = 0; k < S_CONSOLE_WORDS; k++) zw[k] = 0;
+        c.load_scalars(zw);  // idle lanes still hold a defined (never executed) state
+        c.bad_ops = 0; c.status = 0;
     }
     const int w = active ? P.levels[3 * l] : 1, s = active ? P.levels[3 * l + 1] : 1, ar = active ? P.levels[3 * l + 2] : 1;
     // Boot protocol of SuperMarioBrosEnv (fastmario.cpp:422-445), one frame per call of the state machine:
@@ -165,8 +170,11 @@ __global__ void __launch_bounds__(32) k_step(StepParams P) {
     const Fast fst{c.ram, d.prg, d.uop};
     Hot h;
     hot_in(h, c, fst);
-    while (__any_sync(FULL, running)) {
-        if (minpc_turn(running, h) && !hot_step(h, c, fst)) {
+    for (;;) {
+        const uint32_t key = sched_key(running, h);
+        const uint32_t mn = __reduce_min_sync(FULL, key);
+        if (mn == 0xffffffffu) break;
+        if (key == mn && !hot_step(h, c, fst)) {
             hot_out(h, c);
             c.end_frame();
             running = ag.on_frame_end(c, ev, cfg);

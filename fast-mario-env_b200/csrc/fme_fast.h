@@ -42,12 +42,14 @@ struct Fast {
     // side-effect-free read of an address outside $2000-$7FFF
     FME_HD uint32_t M(uint32_t a) const { return a >= 0x8000u ? P(a) : R(a); }
     FME_HD static bool io(uint32_t a) { return a >= 0x2000u && a < 0x8000u; }
+    // micro-op of PRG address pc (masked like every PRG access, so any pc indexes inside the table)
     FME_HD uint2 U(uint32_t pc) const {
+        const uint32_t i = pc & 0x7fffu;
 #if defined(__CUDA_ARCH__)
-        return __ldg(reinterpret_cast<const uint2*>(uop) + (pc - 0x8000u));
+        return __ldg(reinterpret_cast<const uint2*>(uop) + i);
 #else
         uint2 u;
-        u.x = uop[2 * (pc - 0x8000u)]; u.y = uop[2 * (pc - 0x8000u) + 1];
+        u.x = uop[2 * i]; u.y = uop[2 * i + 1];
         return u;
 #endif
     }
@@ -243,28 +245,35 @@ FME_HD void hot_in(Hot& h, const Core& c, const Fast& f) {
 // One scheduling unit of the frame loop (the body of nes_core.hpp:1169-1201) on the register state.
 // Returns false when exec_at reached the frame end (the caller then runs Core::end_frame via hot_out).
 FME_HD bool hot_step(Hot& h, Core& c, const Fast& f) {
-    if (h.exec_at >= FRAME_ITERS) return false;
     const int32_t J = h.exec_at;
-    if (3 * (J + 1) >= h.thresh) {
-        hot_out(h, c);
-        slow_presync(c, J);
-        hot_in(h, c, f);
-        if (h.exec_at != J) return true;  // an NMI was taken before this instruction
-    }
-    // idle-loop test with rd_prg_fast semantics (0xff outside PRG, nes_core.hpp:153, 1178)
-    if (idle_loop(h)) {
-        int32_t lim_end = FRAME_ITERS - J;
-        int32_t lim_nmi = h.thresh - 3 * (J + 1);
-        int32_t k1 = lim_end > 0 ? (lim_end + 2) / 3 : 0;
-        int32_t k2 = lim_nmi > 0 ? (lim_nmi + 8) / 9 : 0;
-        int32_t k = k1 < k2 ? k1 : k2;
-        if (k > 1) {
-            h.exec_at = J + 3 * (k - 1);
-            h.zero_skip = 0;
-            return true;
+    if (J >= FRAME_ITERS) return false;
+    int32_t S;
+    // common case, tested with one branch: no PPU catch-up due, no idle loop, a fast-path micro-op
+    const bool common = (3 * (J + 1) < h.thresh) & ((h.ux & UOP_IDLE) == 0u) & ((h.ux & 0xffu) != H_SLOW);
+    if (common) {
+        S = f.exec(h);
+    } else {
+        if (3 * (J + 1) >= h.thresh) {
+            hot_out(h, c);
+            slow_presync(c, J);
+            hot_in(h, c, f);
+            if (h.exec_at != J) return true;  // an NMI was taken before this instruction
         }
+        // idle-loop test with rd_prg_fast semantics (0xff outside PRG, nes_core.hpp:153, 1178)
+        if (idle_loop(h)) {
+            int32_t lim_end = FRAME_ITERS - J;
+            int32_t lim_nmi = h.thresh - 3 * (J + 1);
+            int32_t k1 = lim_end > 0 ? (lim_end + 2) / 3 : 0;
+            int32_t k2 = lim_nmi > 0 ? (lim_nmi + 8) / 9 : 0;
+            int32_t k = k1 < k2 ? k1 : k2;
+            if (k > 1) {
+                h.exec_at = J + 3 * (k - 1);
+                h.zero_skip = 0;
+                return true;
+            }
+        }
+        S = (h.ux & 0xffu) != H_SLOW ? f.exec(h) : -1;
     }
-    int32_t S = (h.ux & 0xffu) != H_SLOW ? f.exec(h) : -1;
     if (S < 0) {
         const uint32_t opc = h.pc >= 0x8000u ? (h.ux >> 8) & 0xffu : 0x100u;
         hot_out(h, c);

@@ -82,9 +82,15 @@ __device__ __forceinline__ void bind_core(Core& c, const Dev& d, uint8_t* sm, in
 // Lanes spinning in a `JMP *` idle loop wait until every other lane is idle or at the frame boundary, and
 // lanes at the frame boundary wait for all others: the warp then takes the idle fast-forward, the PPU catch-up
 // before the NMI and the frame end together instead of one lane at a time. Returns true if this lane may step.
+// sched_key + __reduce_min_sync: a lane steps when its key is the warp minimum; the minimum is 0xffffffff
+// once no lane is running.
+__device__ __forceinline__ uint32_t sched_key(bool running, const Hot& h) {
+    uint32_t k = h.pc | ((h.ux & UOP_IDLE) ? 0x10000u : 0u);
+    k = h.exec_at >= FRAME_ITERS ? 0x20000u : k;
+    return running ? k : 0xffffffffu;
+}
 __device__ __forceinline__ bool minpc_turn(bool running, const Hot& h) {
-    uint32_t key = 0xffffffffu;
-    if (running) key = h.exec_at >= FRAME_ITERS ? 0x20000u : (idle_loop(h) ? 0x10000u : 0u) | h.pc;
+    const uint32_t key = sched_key(running, h);
     const uint32_t mn = __reduce_min_sync(FULL, key);
     return running && key == mn;
 }

@@ -137,7 +137,7 @@ __device__ __forceinline__ AgentCfg agent_cfg(const StepParams& P) {
 
 __global__ void __launch_bounds__(32) k_step(StepParams P) {
     extern __shared__ __align__(16) uint8_t sm[];
-    const int lane = threadIdx.x, g = blockIdx.x, e = g * 32 + lane;
+    const int lane = threadIdx.x, g = blockIdx.x + P.group_base, e = g * 32 + lane;
     const Dev& d = P.d;
     const bool active = e < d.n;
     const int cap = d.log_cap;
@@ -331,11 +331,12 @@ struct RenderParams {
     const uint32_t* jobs;
     uint8_t* obs; uint8_t* fin;
     int frame_stack;
+    int env_base;   // first env of this launch
 };
 __global__ void __launch_bounds__(32) k_render(RenderParams P) {
     extern __shared__ __align__(16) uint8_t sm[];
     const int lane = threadIdx.x;
-    const int e = blockIdx.x / NBANDS, band = blockIdx.x % NBANDS;
+    const int e = (int)(blockIdx.x / NBANDS) + P.env_base, band = (int)(blockIdx.x % NBANDS);
     const Dev& d = P.d;
     if (e >= d.n) return;
     const uint32_t job = P.jobs[e];
@@ -672,6 +673,8 @@ uint64_t sticky_threshold(double sticky) {
 
 }  // namespace
 
+constexpr int kChunks = 4;
+
 struct FmeEnv {
     FmeConfig cfg{};
     int n = 0, nl = 0, K = 4;
@@ -688,6 +691,12 @@ struct FmeEnv {
     uint8_t* d_cache_obs = nullptr;
     int32_t* d_cache_meta = nullptr;
     uint32_t* d_jobs = nullptr;   // per-env render job of the last step (k_step -> k_render)
+    // A step runs as kChunks slices of the env groups, each an emulation launch on a high-priority stream
+    // followed by its render launch on a low-priority stream: the renders of finished slices fill the SMs
+    // that the slower slices' last warps leave idle. Fork/join with events on the caller's stream.
+    int nch = 0;
+    cudaStream_t s_emu[kChunks] = {}, s_rnd[kChunks] = {};
+    cudaEvent_t ev_in = nullptr, ev_emu[kChunks] = {}, ev_rnd[kChunks] = {};
     FmeBuffers buf{};
     bool bound = false;
     uint64_t sticky_thr = 0;
@@ -713,6 +722,13 @@ static void free_env(FmeEnv* v) {
     v->env.release();
     cudaFree(v->d_level_img); cudaFree(v->d_level_meta); cudaFree(v->d_obs0);
     cudaFree(v->d_cache_img); cudaFree(v->d_cache_obs); cudaFree(v->d_cache_meta); cudaFree(v->d_jobs);
+    for (int c = 0; c < kChunks; c++) {
+        if (v->s_emu[c]) cudaStreamDestroy(v->s_emu[c]);
+        if (v->s_rnd[c]) cudaStreamDestroy(v->s_rnd[c]);
+        if (v->ev_emu[c]) cudaEventDestroy(v->ev_emu[c]);
+        if (v->ev_rnd[c]) cudaEventDestroy(v->ev_rnd[c]);
+    }
+    if (v->ev_in) cudaEventDestroy(v->ev_in);
     delete v;
 }
 
@@ -775,6 +791,19 @@ static int create_impl(const FmeConfig* cfg, const uint8_t* rom, int64_t rom_len
     CK(cudaMalloc(&v->d_lut, 256));
     CK(cudaMalloc(&v->d_err, 4));
     CK(cudaMalloc(&v->d_jobs, (size_t)(C.n_envs + 31) / 32 * 32 * 4));
+    {
+        int lo = 0, hi = 0;
+        CK(cudaDeviceGetStreamPriorityRange(&lo, &hi));
+        const int groups = (C.n_envs + 31) / 32;
+        v->nch = groups < kChunks ? groups : kChunks;
+        CK(cudaEventCreateWithFlags(&v->ev_in, cudaEventDisableTiming));
+        for (int c = 0; c < v->nch; c++) {
+            CK(cudaStreamCreateWithPriority(&v->s_emu[c], cudaStreamNonBlocking, hi));
+            CK(cudaStreamCreateWithPriority(&v->s_rnd[c], cudaStreamNonBlocking, lo));
+            CK(cudaEventCreateWithFlags(&v->ev_emu[c], cudaEventDisableTiming));
+            CK(cudaEventCreateWithFlags(&v->ev_rnd[c], cudaEventDisableTiming));
+        }
+    }
     CK(upload_prg(v->d_prg, prg));
     CK(cudaMemcpy(v->d_chr, chr.data(), 0x2000, cudaMemcpyHostToDevice));
     CK(cudaMemcpy(v->d_lut, gray_lut, 256, cudaMemcpyHostToDevice));
@@ -919,11 +948,26 @@ static int launch_step_like(FmeEnv* v, const int64_t* d_actions, void* stream, b
         k_reset<<<groups, 32, 0, s>>>(P);
     } else {
         P.jobs = v->d_jobs;
-        k_step<<<groups, 32, SLAB_BYTES, s>>>(P);
-        if (mark) CK(cudaEventRecord((cudaEvent_t)mark, s));
         RenderParams R;
         R.d = d; R.jobs = v->d_jobs; R.obs = P.obs; R.fin = P.fin; R.frame_stack = P.frame_stack;
-        k_render<<<(unsigned)v->n * NBANDS, 32, RB_BYTES, s>>>(R);
+        CK(cudaEventRecord(v->ev_in, s));
+        for (int c = 0; c < v->nch; c++) {
+            const int g0 = groups * c / v->nch, g1 = groups * (c + 1) / v->nch;
+            const int e0 = g0 * 32, e1 = g1 * 32 < v->n ? g1 * 32 : v->n;
+            CK(cudaStreamWaitEvent(v->s_emu[c], v->ev_in, 0));
+            P.group_base = g0;
+            k_step<<<g1 - g0, 32, SLAB_BYTES, v->s_emu[c]>>>(P);
+            CK(cudaEventRecord(v->ev_emu[c], v->s_emu[c]));
+            CK(cudaStreamWaitEvent(v->s_rnd[c], v->ev_emu[c], 0));
+            R.env_base = e0;
+            k_render<<<(unsigned)(e1 - e0) * NBANDS, 32, RB_BYTES, v->s_rnd[c]>>>(R);
+            CK(cudaEventRecord(v->ev_rnd[c], v->s_rnd[c]));
+        }
+        if (mark) {  // all emulation slices done (renders may already be running)
+            for (int c = 1; c < v->nch; c++) CK(cudaStreamWaitEvent(v->s_emu[0], v->ev_emu[c], 0));
+            CK(cudaEventRecord((cudaEvent_t)mark, v->s_emu[0]));
+        }
+        for (int c = 0; c < v->nch; c++) CK(cudaStreamWaitEvent(s, v->ev_rnd[c], 0));
     }
     CK(cudaGetLastError());
     return FME_OK;

@@ -55,6 +55,7 @@ struct StepParams {
     int n_levels;
     // MODE_STEP with k_render: per-env render job word (bit 0 active, 1 pooled, 2 slot, 3 episode ended)
     uint32_t* jobs;
+    int group_base;  // first group of this launch (k_step block b handles group group_base + b)
     // MODE_NOOP: where to write the cache entry for this noop step
     uint8_t* out_img; uint8_t* out_obs; int32_t* out_meta; int noop_j;
     const uint8_t* level_img; const uint8_t* level_obs0; const int32_t* level_meta;  // backups (x0, t0)

@@ -52,7 +52,8 @@ def load_package():
 
 
 def workload(args):
-    return dict(workload="config1: synthetic NROM seed 0, 32 levels cycled, skip 4, sticky 0.25, noop_max 30, "
+    name = "config2 (divergence-stress image)" if getattr(args, "divergent", False) else "config1"
+    return dict(workload=f"{name}: synthetic NROM seed 0, 32 levels cycled, skip 4, sticky 0.25, noop_max 30, "
                          "maxpool, max_steps 2000, frame_stack 4, uniform random actions",
                 n_envs_per_gpu=args.envs, skip=4, frame_stack=4, maxpool=True, sticky=0.25, noop_max=30,
                 max_steps=2000, l2="working set per step >> 126 MB L2 (no flush needed)")
@@ -223,6 +224,8 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--divergent", action="store_true",
+                    help="config 2: the divergence-stress image (controller/LFSR-dependent control flow and sprites)")
     ap.add_argument("--ref-gpu", action="store_true",
                     help="also time the reference's CudaVecEnv (baseline/_ref) against this engine at maxpool=False")
     args = ap.parse_args()
@@ -247,7 +250,7 @@ def main():
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
 
     from fast_mario_env_b200 import shard
-    rom = build_rom(0)
+    rom = build_rom(0, divergence=args.divergent)
     E = args.envs
     off = shard.env_offset(rank, E)
     env = fme.CudaVecEnv(level_names(E), E, seed=0, sticky=0.25, noop_max=30, max_steps=2000, skip=4, frame_stack=4,

@@ -142,11 +142,14 @@ __global__ void __launch_bounds__(32) k_step(StepParams P) {
     const bool active = e < d.n;
     const int cap = d.log_cap;
     const AgentCfg cfg = agent_cfg(P);
-    copy_slab(sm, d.slab + (size_t)g * SLAB_BYTES, lane);
+    uint8_t* const gslab = d.slab + (size_t)g * SLAB_BYTES;
+    copy_slab(sm, gslab, lane, STEP_SMEM);
     __syncwarp();
 
     Core c;
     bind_core(c, d, sm, lane, e);
+    c.oam = gslab + SLAB_OAM_OFF + lane * 4;   // OAM and palette stay in HBM (L1-cached)
+    c.pal = gslab + SLAB_PAL_OFF + lane * 4;
     uint32_t w[S_WORDS];
     for (int k = 0; k < S_WORDS; k++) w[k] = 0;
     if (active) load_words(d, e, w);
@@ -235,7 +238,7 @@ __global__ void __launch_bounds__(32) k_step(StepParams P) {
         if (c.status) atomicOr(d.err, c.status);
     }
     __syncwarp();
-    copy_slab(d.slab + (size_t)g * SLAB_BYTES, sm, lane);
+    copy_slab(gslab, sm, lane, STEP_SMEM);
     __syncwarp();
 
     const uint32_t summary = (active ? 1u : 0u) | (pooled ? 2u : 0u) | ((uint32_t)cur_slot << 2) | (ended ? 8u : 0u);
@@ -956,7 +959,7 @@ static int launch_step_like(FmeEnv* v, const int64_t* d_actions, void* stream, b
             const int e0 = g0 * 32, e1 = g1 * 32 < v->n ? g1 * 32 : v->n;
             CK(cudaStreamWaitEvent(v->s_emu[c], v->ev_in, 0));
             P.group_base = g0;
-            k_step<<<g1 - g0, 32, SLAB_BYTES, v->s_emu[c]>>>(P);
+            k_step<<<g1 - g0, 32, STEP_SMEM, v->s_emu[c]>>>(P);
             CK(cudaEventRecord(v->ev_emu[c], v->s_emu[c]));
             CK(cudaStreamWaitEvent(v->s_rnd[c], v->ev_emu[c], 0));
             R.env_base = e0;

@@ -97,12 +97,16 @@ __device__ __forceinline__ bool minpc_turn(bool running, const Hot& h) {
 }
 
 // coalesced copy of a whole slab between HBM and shared memory (warp-wide)
-__device__ __forceinline__ void copy_slab(uint8_t* dst, const uint8_t* src, int lane) {
+__device__ __forceinline__ void copy_slab(uint8_t* dst, const uint8_t* src, int lane, int nbytes = SLAB_BYTES) {
     const uint4* s = reinterpret_cast<const uint4*>(src);
     uint4* d = reinterpret_cast<uint4*>(dst);
 #pragma unroll 4
-    for (int i = lane; i < SLAB_BYTES / 16; i += 32) d[i] = s[i];
+    for (int i = lane; i < nbytes / 16; i += 32) d[i] = s[i];
 }
+// k_step keeps only the group's RAM in shared memory (OAM and palette are used by the rarer PPU paths and
+// stay in the HBM slab, reached through L1): 64 KB per CTA leaves room for a render CTA next to three
+// emulation CTAs on an SM.
+constexpr int STEP_SMEM = SLAB_OAM_OFF;
 
 // ---------------------------------------------------------------- warp renderer
 // Shared-memory layout of the render phase (reuses the emulation slab region).
@@ -188,13 +192,17 @@ __device__ void render_slot(const uint8_t* slot, const RLayout& L, const Dev& d,
             Seg g = decode_seg(rec);
             for (;;) {  // one pass per line of the record
                 if (max_mode && first_row < 0) first_row = g.y;
-                if (g.y < L.row_lo || g.y >= L.row_hi) {         // outside the band
-                    if (g.y >= g.y1) break;
-                    seg_next_line(g);
+                if (g.y >= L.row_hi) break;                        // the rest of the record is below the band
+                if (g.y < L.row_lo) {                              // above the band: jump to its first line
+                    const int to = L.row_lo < g.y1 ? L.row_lo : g.y1;
+                    if (to <= g.y) break;                          // the record ends above the band
+                    seg_skip_lines(g, to - g.y);
                     continue;
                 }
-                uint32_t nsl, lo, hi;
-                if (g.pend) {
+                uint32_t nsl = 0, lo = 0, hi = 0;
+                if (!(g.flags & RF_SHOW_SPR)) {
+                    // sprites hidden: no list needed
+                } else if (g.pend) {
                     uint32_t key = g.ev_y | (g.oam_addr << 8) | ((g.flags & RF_LONG) ? 0x10000u : 0u) | (ver << 17);
                     if (key != lkey) {
                         int start = (int)(g.oam_addr >> 2);

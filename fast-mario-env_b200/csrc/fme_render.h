@@ -95,6 +95,28 @@ FME_HD void seg_next_line(Seg& g) {
     g.pend = 1u; g.ev_y = (uint32_t)g.y;
     g.y++; g.x0 = 0; g.x1 = g.y == g.y1 ? g.xe : 256;
 }
+// L >= 1 applications of seg_next_line in closed form (whole lines after the first add 32 coarse-x
+// increments, one fine-y increment and the copy of t's x bits each).
+FME_HD void seg_skip_lines(Seg& g, int L) {
+    if (L == 1) { seg_next_line(g); return; }
+    if (g.flags & RF_SHOW_BG) {
+        uint32_t v = g.v;
+        const uint32_t tot = (v & 0x1fu) + (uint32_t)inc_count_fx(g.fine_x, g.x0, 256);
+        v = (v & ~0x1fu & 0xffffu) | (tot & 31u);
+        if ((tot >> 5) & 1u) v ^= 0x0400u;
+        if (g.flags & RF_SHOW_SPR) {
+            v = fine_y_add(v, L);
+            v = (v & ~0x041fu & 0xffffu) | g.tx;
+        } else {
+            if ((L - 1) & 1) v ^= 0x0400u;
+            v = fine_y_add(v, L);
+        }
+        g.v = v;
+    }
+    g.y += L;
+    g.pend = 1u; g.ev_y = (uint32_t)(g.y - 1);
+    g.x0 = 0; g.x1 = g.y == g.y1 ? g.xe : 256;
+}
 
 // v after n coarse-x increments (nes_core.hpp:310-315 applied n times in closed form)
 FME_HD uint32_t v_after(uint32_t v, int n) {

@@ -198,8 +198,93 @@ def reference_cuda(rom, E, steps, warmup, dev):
     return out
 
 
+def run_ppo(args, rank, world, dev, dist):
+    """PPO samples/s — rollouts on this engine (4096 envs per GPU x 128 steps) and the update
+    (GAE kernel, 4 epochs of minibatch 1024 with advantage normalisation kernel, Nature-CNN fwd/bwd, Adam, CUDA
+    graph; gradients averaged over ranks with NCCL). Device-timed with CUDA events, max over ranks."""
+    import torch
+    fme = load_package()
+    from fast_mario_env_b200 import ppo, shard
+    from fast_mario_env_b200.synth_rom import build_rom
+    E = args.ppo_envs
+    rom = build_rom(0)
+    env = fme.CudaVecEnv(level_names(E), E, seed=0, sticky=0.25, noop_max=30, max_steps=2000, skip=4, frame_stack=4,
+                         maxpool=True, device=dev, rom=rom, env_offset=shard.env_offset(rank, E))
+    cfg = ppo.PPOConfig(n_envs=E, n_steps=128, batch=1024, epochs=4)
+    tr = ppo.Trainer(env, cfg, dev, seed=rank)
+    iters = max(1, args.steps // 5)
+    for _ in range(1):
+        tr.iterate()  # warm-up (cudnn autotune, graph pools)
+    torch.cuda.synchronize(dev)
+    if dist:
+        dist.barrier()
+    e0, e1, em = (torch.cuda.Event(enable_timing=True) for _ in range(3))
+    coll = 0.0
+    e0.record()
+    for _ in range(iters):
+        c0, c1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        c0.record(); tr.collect(); c1.record()
+        tr.L.update()
+        c1.synchronize()
+        coll += c0.elapsed_time(c1)
+    e1.record()
+    torch.cuda.synchronize(dev)
+    ms = e0.elapsed_time(e1)
+    ms_max = shard.max_over_ranks(ms, device=dev)
+    samples = world * E * cfg.n_steps * iters
+    if rank == 0:
+        print(json.dumps({"metric": "PPO samples/sec (config 4)", "value": samples / (ms_max / 1000.0), "unit": "samples/s",
+                          "n_gpus": world, "iterations": iters, "ms_per_iteration": ms_max / iters,
+                          "rollout_ms_per_iteration": coll / iters, "higher_is_better": True, "scaling": "weak",
+                          "dtype": "fp32", "data": "synthetic",
+                          "config": {"workload": "config4: Nature-CNN PPO on config-1 envs", "n_envs_per_gpu": E,
+                                     "n_steps": 128, "epochs": 4, "minibatch": 1024, "gamma": 0.99, "lam": 0.95,
+                                     "parallelism": f"dp{world} (NCCL gradient all-reduce)" if world > 1 else "dp1"}}))
+    env.close()
+
+
+def run_reference_ppo(args):
+    """The reference trainer itself (baseline/_ref, `python -m fast_mario_env.ppo.train`, unmodified) in its
+    throughput mode on its CUDA env backend with the config-4 hyper-parameters and this synthetic ROM; its
+    reported fps (env steps = samples per second) is the line's value."""
+    ref_dir = os.path.join(ROOT, "baseline", "_ref")
+    if not os.path.isdir(os.path.join(ref_dir, "fast_mario_env")):
+        print(json.dumps({"impl": "reference", "unavailable": "baseline/_ref not installed"}))
+        return
+    load_package()
+    from fast_mario_env_b200.synth_rom import build_rom
+    with tempfile.NamedTemporaryFile(suffix=".nes", delete=False) as f:
+        f.write(build_rom(0))
+        rom_path = f.name
+    cmd = [sys.executable, "-m", "fast_mario_env.ppo.train", "--env-backend", "cuda", "--n-envs", str(args.ppo_envs),
+           "--groups", "1", "--n-steps", "128", "--batch", "1024", "--epochs", "4", "--gamma", "0.99", "--lam", "0.95",
+           "--bench", str(max(10, 4 * args.steps)), "--eval-every", "1e12", "--no-tb", "--rom", rom_path]
+    env = dict(os.environ, PYTHONPATH=ref_dir + os.pathsep + os.environ.get("PYTHONPATH", ""))
+    try:
+        r = subprocess.run(cmd, env=env, capture_output=True, text=True, timeout=1200)
+    finally:
+        os.unlink(rom_path)
+    done = [l for l in r.stdout.splitlines() if l.startswith("DONE ")]
+    if r.returncode != 0 or not done:
+        print(json.dumps({"impl": "reference", "unavailable": f"reference trainer failed (rc {r.returncode}): "
+                                                              f"{(r.stderr or r.stdout).strip().splitlines()[-1:]}"}))
+        return
+    res = json.loads(done[-1][5:])
+    print(json.dumps({"impl": "reference", "metric": "PPO samples/sec (config 4)", "value": float(res["fps"]),
+                      "unit": "samples/s", "n_gpus": 1, "higher_is_better": True, "scaling": "weak", "dtype": "fp32",
+                      "data": "synthetic", "config": {"workload": "config4 via the reference trainer (cuda env backend, "
+                                                                  "maxpool off: the only setting it supports)",
+                                                      "n_envs_per_gpu": args.ppo_envs, "n_steps": 128, "epochs": 4,
+                                                      "minibatch": 1024},
+                      "e2e": {"value": float(res["fps"]), "unit": "samples/s", "h2d_bytes_per_step": 0,
+                              "d2h_bytes_per_step": 0}}))
+
+
 def run_reference(args, rank):
     if rank != 0:
+        return
+    if args.ppo:
+        run_reference_ppo(args)
         return
     load_package()
     from fast_mario_env_b200.synth_rom import build_rom
@@ -224,6 +309,8 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--ppo", action="store_true", help="config 4: PPO samples/s instead of env-steps/s")
+    ap.add_argument("--ppo-envs", type=int, default=4096)
     ap.add_argument("--divergent", action="store_true",
                     help="config 2: the divergence-stress image (controller/LFSR-dependent control flow and sprites)")
     ap.add_argument("--ref-gpu", action="store_true",
@@ -250,6 +337,12 @@ def main():
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
 
     from fast_mario_env_b200 import shard
+    if args.ppo:
+        run_ppo(args, rank, world, dev, dist)
+        if dist:
+            dist.barrier()
+            dist.destroy_process_group()
+        return
     rom = build_rom(0, divergence=args.divergent)
     E = args.envs
     off = shard.env_offset(rank, E)

@@ -51,6 +51,8 @@ SIGNATURES = {
     "fme_raw_destroy": (None, [_P]),
     "fme_raw_frame_static": (_i32, [_P, _P, _P, _i32, _P]),
     "fme_step_marked": (_i32, [_P, _P, _P, _P]),
+    "fme_gae": (_i32, [_P, _P, _P, _P, _P, _i32, _i32, ctypes.c_float, ctypes.c_float, _P, _P, _P]),
+    "fme_adv_norm": (_i32, [_P, _P, _i32, _P]),
     "fme_palette": (None, [_P]),
     "fme_resize": (_i32, [_P, _P, _i32, _P]),
     "fme_state_bytes": (_i64, []),

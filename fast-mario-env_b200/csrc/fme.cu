@@ -20,6 +20,7 @@
 #include <vector>
 
 #include "fme_kernels.cuh"
+#include "fme_ppo.cuh"
 #include "../../include/fme.h"
 #include "fme_tables.h"
 
@@ -1165,6 +1166,24 @@ int fme_raw_frame_static(FmeRaw* r, const uint8_t* d_buttons, uint8_t* d_screens
     P.d.log_cap = FME_STATIC_LOG_CAPACITY;
     P.buttons = d_buttons; P.render = render ? 1 : 0; P.screens = d_screens;
     k_raw<<<(r->n + 31) / 32, 32, SLAB_BYTES, (cudaStream_t)stream>>>(P);
+    CK(cudaGetLastError());
+    return FME_OK;
+}
+
+// ---------------------------------------------------------------- PPO data kernels
+int fme_gae(const float* d_rew, const float* d_val, const float* d_done, const float* d_next_val,
+            const float* d_next_done, int32_t T, int32_t N, float gamma, float gamma_lam, float* d_adv, float* d_ret,
+            void* stream) {
+    if (!d_rew || !d_val || !d_done || !d_next_val || !d_next_done || !d_adv || !d_ret || T < 1 || N < 1)
+        return fail(FME_E_ARG, "bad GAE arguments");
+    k_gae<<<(N + 255) / 256, 256, 0, (cudaStream_t)stream>>>(d_rew, d_val, d_done, d_next_val, d_next_done, T, N,
+                                                             gamma, gamma_lam, d_adv, d_ret);
+    CK(cudaGetLastError());
+    return FME_OK;
+}
+int fme_adv_norm(const float* d_in, float* d_out, int32_t n, void* stream) {
+    if (!d_in || !d_out || n < 1) return fail(FME_E_ARG, "bad advantage-normalisation arguments");
+    k_adv_norm<<<1, ADV_THREADS, 0, (cudaStream_t)stream>>>(d_in, d_out, n);
     CK(cudaGetLastError());
     return FME_OK;
 }

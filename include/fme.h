@@ -158,6 +158,18 @@ void fme_palette(uint32_t* out64);
 /* 240x256 gray -> 84x84 INTER_AREA on the device, n images, async (replaces fm_resize_fast,
  * csrc/fastmario.cpp:643-649, with the same float operation order). */
 int fme_resize(const uint8_t* d_src, uint8_t* d_dst, int32_t n, void* stream);
+/* ---- PPO trainer data kernels (the network stays in torch) ---- */
+/* GAE over a (T, N) rollout, replacing Learner._gae (src/fast_mario_env/ppo/train.py:148-160): fp32 rew, val,
+ * done (1 = obs[t] starts a new episode) of shape (T, N), next_val / next_done (N,); writes adv and
+ * ret = adv + val (T, N). gamma and gamma_lam = gamma*lam (computed in double, then rounded) as fp32 scalars.
+ * Same fp32 operations in the same order as the reference. Async. */
+int fme_gae(const float* d_rew, const float* d_val, const float* d_done, const float* d_next_val,
+            const float* d_next_done, int32_t T, int32_t N, float gamma, float gamma_lam, float* d_adv, float* d_ret,
+            void* stream);
+/* Minibatch advantage normalisation of ppo_loss (src/fast_mario_env/ppo/model.py:61-62):
+ * out = (in - mean) / (std + 1e-8), unbiased std, n values (in == out allowed). Async. */
+int fme_adv_norm(const float* d_in, float* d_out, int32_t n, void* stream);
+
 /* Console state size in bytes of the reset-cache image (cf. fm_state_bytes, csrc/fastmario.cpp:631). */
 int64_t fme_state_bytes(void);
 const char* fme_last_error(void);

@@ -53,6 +53,8 @@ SIGNATURES = {
     "fme_step_marked": (_i32, [_P, _P, _P, _P]),
     "fme_gae": (_i32, [_P, _P, _P, _P, _P, _i32, _i32, ctypes.c_float, ctypes.c_float, _P, _P, _P]),
     "fme_adv_norm": (_i32, [_P, _P, _i32, _P]),
+    "fme_replay_add": (_i32, [_P, _P, _P, _i32, _P, _P, _P, _P, _P]),
+    "fme_replay_gather": (_i32, [_P, _P, _P, _i32, _i32, _i32, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P]),
     "fme_palette": (None, [_P]),
     "fme_resize": (_i32, [_P, _P, _i32, _P]),
     "fme_state_bytes": (_i64, []),
@@ -65,6 +67,11 @@ class FmeConfig(ctypes.Structure):
     _fields_ = [("n_envs", _i32), ("skip", _i32), ("max_steps", _i32), ("noop_max", _i32), ("maxpool", _i32),
                 ("frame_stack", _i32), ("sticky", _dbl), ("device", _i32), ("log_capacity", _i32),
                 ("hack_cap", _i32), ("boot_cap", _i32)]
+
+
+class FmeReplayBufs(ctypes.Structure):
+    _fields_ = [(f, _P) for f in ("frames", "age", "act", "rew", "flags", "ptr", "new_ep")] + \
+               [("n_envs", _i32), ("capacity", _i32)]
 
 
 class FmeBuffers(ctypes.Structure):

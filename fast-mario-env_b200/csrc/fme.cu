@@ -21,6 +21,7 @@
 
 #include "fme_kernels.cuh"
 #include "fme_ppo.cuh"
+#include "fme_replay.cuh"
 #include "../../include/fme.h"
 #include "fme_tables.h"
 
@@ -1184,6 +1185,47 @@ int fme_gae(const float* d_rew, const float* d_val, const float* d_done, const f
 int fme_adv_norm(const float* d_in, float* d_out, int32_t n, void* stream) {
     if (!d_in || !d_out || n < 1) return fail(FME_E_ARG, "bad advantage-normalisation arguments");
     k_adv_norm<<<1, ADV_THREADS, 0, (cudaStream_t)stream>>>(d_in, d_out, n);
+    CK(cudaGetLastError());
+    return FME_OK;
+}
+
+// ---------------------------------------------------------------- frame-deduplicating replay buffer
+static int replay_dev(const FmeReplayBufs* rb, ReplayDev* out) {
+    if (!rb || !rb->frames || !rb->age || !rb->act || !rb->rew || !rb->flags || !rb->ptr || !rb->new_ep ||
+        rb->n_envs < 1 || rb->capacity < 1)
+        return fail(FME_E_ARG, "bad replay buffers");
+    if ((uintptr_t)rb->frames & 15) return fail(FME_E_ARG, "replay frames must be 16-byte aligned");
+    out->frames = rb->frames; out->age = rb->age; out->act = rb->act; out->rew = rb->rew; out->flags = rb->flags;
+    out->ptr = rb->ptr; out->new_ep = rb->new_ep; out->E = rb->n_envs; out->C = rb->capacity;
+    return FME_OK;
+}
+int fme_replay_add(const FmeReplayBufs* rb, const uint8_t* d_obs, const uint8_t* d_next_obs, int32_t k,
+                   const int64_t* d_action, const float* d_reward, const uint8_t* d_done, const uint8_t* d_trunc,
+                   void* stream) {
+    ReplayDev R;
+    int rc = replay_dev(rb, &R);
+    if (rc) return rc;
+    if (!d_obs || !d_next_obs || !d_action || !d_reward || !d_done || !d_trunc || k < 1)
+        return fail(FME_E_ARG, "bad replay add arguments");
+    if (((uintptr_t)d_obs & 15) || ((uintptr_t)d_next_obs & 15)) return fail(FME_E_ARG, "obs must be 16-byte aligned");
+    k_replay_add<<<R.E, 32, 0, (cudaStream_t)stream>>>(R, d_obs, d_next_obs, d_action, d_reward, d_done, d_trunc, k);
+    CK(cudaGetLastError());
+    return FME_OK;
+}
+int fme_replay_gather(const FmeReplayBufs* rb, const int64_t* d_env, const int64_t* d_pos, int32_t B, int32_t k,
+                      int32_t n_step, const float* d_gpow, const float* d_dpow, uint8_t* d_obs, uint8_t* d_next_obs,
+                      int64_t* d_act, float* d_reward, float* d_discount, float* d_terminal, int64_t* d_steps,
+                      void* stream) {
+    ReplayDev R;
+    int rc = replay_dev(rb, &R);
+    if (rc) return rc;
+    if (!d_env || !d_pos || !d_gpow || !d_dpow || !d_obs || !d_next_obs || !d_act || !d_reward || !d_discount ||
+        !d_terminal || !d_steps || B < 0 || k < 1 || n_step < 1 || n_step > R.C)
+        return fail(FME_E_ARG, "bad replay gather arguments");
+    if (((uintptr_t)d_obs & 15) || ((uintptr_t)d_next_obs & 15)) return fail(FME_E_ARG, "obs must be 16-byte aligned");
+    if (B == 0) return FME_OK;
+    k_replay_gather<<<B, 32, 0, (cudaStream_t)stream>>>(R, d_env, d_pos, B, k, n_step, d_gpow, d_dpow, d_obs,
+                                                        d_next_obs, d_act, d_reward, d_discount, d_terminal, d_steps);
     CK(cudaGetLastError());
     return FME_OK;
 }

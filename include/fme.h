@@ -170,6 +170,32 @@ int fme_gae(const float* d_rew, const float* d_val, const float* d_done, const f
  * out = (in - mean) / (std + 1e-8), unbiased std, n values (in == out allowed). Async. */
 int fme_adv_norm(const float* d_in, float* d_out, int32_t n, void* stream);
 
+/* ---- frame-deduplicating replay buffer (replaces FrameReplay's add / sample gathers,
+ *      src/fast_mario_env/replay.py:69-139); caller-owned device storage, a ring of `capacity` slots per env ---- */
+typedef struct FmeReplayBufs {
+    uint8_t* frames;   /* (n_envs, capacity, 84, 84), 16-byte aligned */
+    uint8_t* age;      /* (n_envs, capacity) frames since the episode start, saturating at 255 */
+    int16_t* act;      /* (n_envs, capacity) */
+    float* rew;        /* (n_envs, capacity) */
+    uint8_t* flags;    /* (n_envs, capacity) 1 valid start, 2 done, 4 terminal */
+    int64_t* ptr;      /* (n_envs,) slots written per env */
+    uint8_t* new_ep;   /* (n_envs,) 1 = the next add starts an episode (start at 1) */
+    int32_t n_envs;
+    int32_t capacity;
+} FmeReplayBufs;
+/* One transition per env (FrameReplay.add): obs / next_obs (n_envs, k, 84, 84) uint8 (frame k-1 is stored),
+ * action int64, reward float32, done / trunc uint8 (n_envs,). Async. */
+int fme_replay_add(const FmeReplayBufs* rb, const uint8_t* d_obs, const uint8_t* d_next_obs, int32_t k,
+                   const int64_t* d_action, const float* d_reward, const uint8_t* d_done, const uint8_t* d_trunc,
+                   void* stream);
+/* The batch of FrameReplay.sample for sampled (env, pos) pairs: stacks at pos and pos+m with frames before the
+ * episode start zeroed, action, n-step reward, discount gamma^m * (1 - terminal), terminal, m. gpow[i] = gamma^i
+ * (i < n_step) and dpow[m] = gamma^m (m <= n_step) as float32 tables. Async. */
+int fme_replay_gather(const FmeReplayBufs* rb, const int64_t* d_env, const int64_t* d_pos, int32_t B, int32_t k,
+                      int32_t n_step, const float* d_gpow, const float* d_dpow, uint8_t* d_obs, uint8_t* d_next_obs,
+                      int64_t* d_act, float* d_reward, float* d_discount, float* d_terminal, int64_t* d_steps,
+                      void* stream);
+
 /* Console state size in bytes of the reset-cache image (cf. fm_state_bytes, csrc/fastmario.cpp:631). */
 int64_t fme_state_bytes(void);
 const char* fme_last_error(void);

@@ -207,6 +207,7 @@ def run_ppo(args, rank, world, dev, dist):
     from fast_mario_env_b200 import ppo, shard
     from fast_mario_env_b200.synth_rom import build_rom
     E = args.ppo_envs
+    torch.backends.cudnn.benchmark = True   # as the reference trainer (train.py main)
     rom = build_rom(0)
     env = fme.CudaVecEnv(level_names(E), E, seed=0, sticky=0.25, noop_max=30, max_steps=2000, skip=4, frame_stack=4,
                          maxpool=True, device=dev, rom=rom, env_offset=shard.env_offset(rank, E))

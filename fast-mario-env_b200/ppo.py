@@ -38,6 +38,7 @@ class PPOConfig:
     adam_eps: float = 1e-5
     max_grad_norm: float = 0.5
     graph: bool = True
+    channels_last: bool = True   # NHWC activations and weights for the convolutions (the reference's default)
 
 
 class NatureAC(nn.Module):
@@ -60,15 +61,17 @@ class NatureAC(nn.Module):
         nn.init.orthogonal_(self.vf.weight, 1.0)
         nn.init.zeros_(self.vf.bias)
 
-    def forward(self, obs_u8):
+    def forward(self, obs_u8, channels_last: bool = False):
         x = obs_u8.float().mul_(1.0 / 255.0)
+        if channels_last:
+            x = x.contiguous(memory_format=torch.channels_last)
         h = F.relu(self.fc(self.cnn(x)))
         return self.pi(h), self.vf(h).squeeze(-1)
 
     @torch.no_grad()
-    def act(self, obs_u8):
+    def act(self, obs_u8, channels_last: bool = False):
         """Gumbel-max sample of the policy (graph-capturable): action int64, its log-prob, value."""
-        logits, v = self(obs_u8)
+        logits, v = self(obs_u8, channels_last)
         logp_all = F.log_softmax(logits, -1)
         u = torch.rand_like(logits).clamp_(1e-20, 1.0)
         a = (logp_all - torch.log(-torch.log(u))).argmax(-1)
@@ -96,11 +99,11 @@ def adv_norm(x, out=None):
     return out
 
 
-def ppo_loss(net, obs, act, old_logp, adv_n, ret, clip, ent_coef, vf_coef):
+def ppo_loss(net, obs, act, old_logp, adv_n, ret, clip, ent_coef, vf_coef, channels_last=False):
     """The reference loss (model.py:55-74) with the advantages already normalised by `adv_norm`: clipped
     surrogate, unclipped MSE value loss, -mean(entropy); stats as the reference (pg, vf, entropy, clip
     fraction, approx kl)."""
-    logits, v = net(obs)
+    logits, v = net(obs, channels_last)
     logp_all = F.log_softmax(logits, -1)
     logp = logp_all.gather(-1, act[:, None]).squeeze(-1)
     ent = -(logp_all.exp() * logp_all).sum(-1)
@@ -119,14 +122,14 @@ def average_grads(params, flat, world):
     """Data-parallel gradient mean: pack every gradient into one flat buffer, one all-reduce (sum) over the
     default process group, divide by the world size, unpack."""
     off = 0
-    for p in params:
-        flat[off:off + p.numel()].copy_(p.grad.view(-1))
+    for p in params:  # reshape / view_as keep the logical order whatever the memory format (channels-last)
+        flat[off:off + p.numel()].copy_(p.grad.reshape(-1))
         off += p.numel()
     torch.distributed.all_reduce(flat)
     flat.div_(world)
     off = 0
     for p in params:
-        p.grad.view(-1).copy_(flat[off:off + p.numel()])
+        p.grad.copy_(flat[off:off + p.numel()].view(p.grad.shape))
         off += p.numel()
 
 
@@ -149,6 +152,8 @@ class Learner:
         self.cfg, self.dev = cfg, dev
         T, n = cfg.n_steps, cfg.n_envs
         self.net = (net if net is not None else NatureAC(7)).to(dev)
+        if cfg.channels_last:
+            self.net = self.net.to(memory_format=torch.channels_last)
         self.params = list(self.net.parameters())
         self.world = torch.distributed.get_world_size() if torch.distributed.is_initialized() else 1
         self.opt = torch.optim.Adam(self.params, lr=torch.tensor(cfg.lr, device=dev) if cfg.graph else cfg.lr,
@@ -173,7 +178,7 @@ class Learner:
         obs = b.obs.view(-1, 4, 84, 84)[i]
         adv_norm(self.adv.view(-1)[i], self.adv_mb)
         loss, st = ppo_loss(self.net, obs, b.act.view(-1)[i], b.logp.view(-1)[i], self.adv_mb, self.ret.view(-1)[i],
-                            c.clip, c.ent, c.vf)
+                            c.clip, c.ent, c.vf, channels_last=c.channels_last)
         self.opt.zero_grad(set_to_none=not c.graph)
         loss.backward()
         return st
@@ -267,7 +272,7 @@ class Trainer:
                 self._policy()
 
     def _policy(self):
-        a, lp, v = self.L.net.act(self.inp)
+        a, lp, v = self.L.net.act(self.inp, self.cfg.channels_last)
         self.a.copy_(a); self.lp.copy_(lp); self.v.copy_(v)
 
     def collect(self):
@@ -288,11 +293,11 @@ class Trainer:
             if bool(tmask.any()):  # rare (time limit): one small sync
                 ti = tmask.nonzero().squeeze(-1)
                 with torch.no_grad():
-                    _, v = self.L.net(info["final_obs"][ti])
+                    _, v = self.L.net(info["final_obs"][ti], c.channels_last)
                 b.rew[t, ti] += c.gamma * v
         self.obs = self.inp
         with torch.no_grad():
-            _, nv = self.L.net(self.inp)
+            _, nv = self.L.net(self.inp, c.channels_last)
         b.next_val.copy_(nv)
 
     def iterate(self):

@@ -92,13 +92,13 @@ def test_loss_gradients_and_adam_step_match_reference(g):
     norms = np.array([p.grad.double().norm().item() for p in L.params])
     np.testing.assert_allclose(norms, g["grad_norms"], rtol=1e-4)
     for k, p in enumerate(L.params):
-        got = p.grad.view(-1)[torch.from_numpy(g["grad_idx"][k]).cuda()].double().cpu().numpy()
+        got = p.grad.reshape(-1)[torch.from_numpy(g["grad_idx"][k]).cuda()].double().cpu().numpy()
         np.testing.assert_allclose(got, g["grad_val"][k], rtol=1e-4, atol=1e-4 * float(g["grad_norms"][k]) / 50)
     # the captured minibatch step: clip + Adam from the restored state
     L.minibatch(torch.arange(mg.B, device="cuda"))
     torch.cuda.synchronize()
     for k, (p, q) in enumerate(zip(L.params, before)):
-        d = (p.detach() - q).view(-1)[torch.from_numpy(g["grad_idx"][k]).cuda()].double().cpu().numpy()
+        d = (p.detach() - q).reshape(-1)[torch.from_numpy(g["grad_idx"][k]).cuda()].double().cpu().numpy()
         np.testing.assert_allclose(d, g["step_delta"][k], rtol=1e-3, atol=2e-7)
 
 

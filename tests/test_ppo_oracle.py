@@ -62,12 +62,16 @@ def _avg_worker(rank, world):
     os.environ.setdefault("MASTER_PORT", "29561")
     dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60))
     try:
-        ps = [torch.nn.Parameter(torch.zeros(3, 2)), torch.nn.Parameter(torch.zeros(5))]
+        ps = [torch.nn.Parameter(torch.zeros(3, 2)), torch.nn.Parameter(torch.zeros(5)),
+              torch.nn.Parameter(torch.zeros(2, 3, 2, 2).to(memory_format=torch.channels_last))]
         ps[0].grad = torch.full((3, 2), float(rank + 1))
         ps[1].grad = torch.arange(5, dtype=torch.float32) * (rank + 1)
-        flat = torch.zeros(11)
+        g2 = torch.arange(24, dtype=torch.float32).view(2, 3, 2, 2) * (rank + 1)
+        ps[2].grad = g2.contiguous(memory_format=torch.channels_last)
+        flat = torch.zeros(35)
         ppo.average_grads(ps, flat, world)
         assert torch.allclose(ps[0].grad, torch.full((3, 2), 1.5))
         assert torch.allclose(ps[1].grad, torch.arange(5, dtype=torch.float32) * 1.5)
+        assert torch.allclose(ps[2].grad, torch.arange(24, dtype=torch.float32).view(2, 3, 2, 2) * 1.5)
     finally:
         dist.destroy_process_group()

@@ -51,6 +51,7 @@ SIGNATURES = {
     "fme_raw_destroy": (None, [_P]),
     "fme_raw_frame_static": (_i32, [_P, _P, _P, _i32, _P]),
     "fme_step_marked": (_i32, [_P, _P, _P, _P]),
+    "fme_step_to_host": (_i32, [_P, _P, _P, _P]),
     "fme_gae": (_i32, [_P, _P, _P, _P, _P, _i32, _i32, ctypes.c_float, ctypes.c_float, _P, _P, _P]),
     "fme_adv_norm": (_i32, [_P, _P, _i32, _P]),
     "fme_replay_add": (_i32, [_P, _P, _P, _i32, _P, _P, _P, _P, _P]),
@@ -67,6 +68,10 @@ class FmeConfig(ctypes.Structure):
     _fields_ = [("n_envs", _i32), ("skip", _i32), ("max_steps", _i32), ("noop_max", _i32), ("maxpool", _i32),
                 ("frame_stack", _i32), ("sticky", _dbl), ("device", _i32), ("log_capacity", _i32),
                 ("hack_cap", _i32), ("boot_cap", _i32)]
+
+
+class FmeHostOut(ctypes.Structure):
+    _fields_ = [(f, _P) for f in ("obs", "rew", "term", "trunc", "info", "ep_ret", "ep_len")]
 
 
 class FmeReplayBufs(ctypes.Structure):

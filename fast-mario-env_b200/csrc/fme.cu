@@ -936,7 +936,8 @@ int fme_set_buffers(FmeEnv* v, const FmeBuffers* b) {
     return FME_OK;
 }
 
-static int launch_step_like(FmeEnv* v, const int64_t* d_actions, void* stream, bool reset, void* mark = nullptr) {
+static int launch_step_like(FmeEnv* v, const int64_t* d_actions, void* stream, bool reset, void* mark = nullptr,
+                            const FmeHostOut* host = nullptr) {
     if (!v) return fail(FME_E_ARG, "null env");
     if (!v->bound) return fail(FME_E_STATE, "fme_set_buffers must be called first");
     if (!reset && !d_actions) return fail(FME_E_ARG, "null actions");
@@ -966,6 +967,17 @@ static int launch_step_like(FmeEnv* v, const int64_t* d_actions, void* stream, b
             CK(cudaStreamWaitEvent(v->s_rnd[c], v->ev_emu[c], 0));
             R.env_base = e0;
             k_render<<<(unsigned)(e1 - e0) * NBANDS, 32, RB_BYTES, v->s_rnd[c]>>>(R);
+            if (host) {  // this slice's outputs to the host while later slices still run
+                const size_t ob = (size_t)v->K * OBS_BYTES, ne = (size_t)(e1 - e0);
+                cudaStream_t cs = v->s_rnd[c];
+                CK(cudaMemcpyAsync(host->obs + e0 * ob, P.obs + e0 * ob, ne * ob, cudaMemcpyDeviceToHost, cs));
+                CK(cudaMemcpyAsync(host->rew + e0, P.rew + e0, ne * 4, cudaMemcpyDeviceToHost, cs));
+                CK(cudaMemcpyAsync(host->term + e0, P.term + e0, ne, cudaMemcpyDeviceToHost, cs));
+                CK(cudaMemcpyAsync(host->trunc + e0, P.trunc + e0, ne, cudaMemcpyDeviceToHost, cs));
+                CK(cudaMemcpyAsync(host->info + e0 * 10, P.info + e0 * 10, ne * 40, cudaMemcpyDeviceToHost, cs));
+                CK(cudaMemcpyAsync(host->ep_ret + e0, P.ep_ret + e0, ne * 8, cudaMemcpyDeviceToHost, cs));
+                CK(cudaMemcpyAsync(host->ep_len + e0, P.ep_len + e0, ne * 4, cudaMemcpyDeviceToHost, cs));
+            }
             CK(cudaEventRecord(v->ev_rnd[c], v->s_rnd[c]));
         }
         if (mark) {  // all emulation slices done (renders may already be running)
@@ -980,6 +992,11 @@ static int launch_step_like(FmeEnv* v, const int64_t* d_actions, void* stream, b
 
 int fme_reset(FmeEnv* v, void* stream) { return launch_step_like(v, nullptr, stream, true); }
 int fme_step(FmeEnv* v, const int64_t* d_actions, void* stream) { return launch_step_like(v, d_actions, stream, false); }
+int fme_step_to_host(FmeEnv* v, const int64_t* d_actions, const FmeHostOut* out, void* stream) {
+    if (!out || !out->obs || !out->rew || !out->term || !out->trunc || !out->info || !out->ep_ret || !out->ep_len)
+        return fail(FME_E_ARG, "all host outputs are required");
+    return launch_step_like(v, d_actions, stream, false, nullptr, out);
+}
 int fme_step_marked(FmeEnv* v, const int64_t* d_actions, void* stream, void* event) {
     if (!event) return fail(FME_E_ARG, "null event");
     return launch_step_like(v, d_actions, stream, false, event);

@@ -249,6 +249,8 @@ class FastVecEnv:
         self._epr = torch.zeros(n_envs, dtype=torch.float64, **pin)
         self._epl = torch.zeros(n_envs, dtype=torch.int32, **pin)
         self._event = torch.cuda.Event()
+        self._hout = N.FmeHostOut(*[t.data_ptr() for t in (self._obs, self._rew, self._term, self._trunc, self._info,
+                                                            self._epr, self._epl)])
         self.monitor = MonitorCSV(monitor_path) if monitor_path else None
         self.t0 = time.time()
         self._pending = False
@@ -279,12 +281,11 @@ class FastVecEnv:
         if a.shape[0] != self.n:
             raise ValueError(f"expected {self.n} actions, got {a.shape[0]}")
         self._act.numpy()[:] = a
-        self.env.actions.copy_(self._act, non_blocking=True)
-        self.env.step(self.env.actions)
         e = self.env
-        for dst, src in ((self._obs, e.obs), (self._rew, e.rew), (self._term, e.term), (self._trunc, e.trunc),
-                         (self._info, e.info_t), (self._epr, e.ep_ret), (self._epl, e.ep_len)):
-            dst.copy_(src, non_blocking=True)
+        e.actions.copy_(self._act, non_blocking=True)
+        # the step, with each env slice's outputs copied to the pinned host arrays as soon as it is done
+        N.check(N.lib().fme_step_to_host(e.h, N.ptr(e.actions), ctypes.byref(self._hout), e._stream()),
+                "fme_step_to_host")
         self._event.record()
         self._pending = True
 

@@ -102,6 +102,22 @@ int fme_step(FmeEnv* env, const int64_t* d_actions, void* stream);
  * reference (a profiling hook; the step itself is identical). */
 int fme_step_marked(FmeEnv* env, const int64_t* d_actions, void* stream, void* event);
 
+/* Pinned host destinations of fme_step_to_host (shapes as FmeBuffers; final_obs stays on the device). */
+typedef struct FmeHostOut {
+    uint8_t* obs;
+    float* rew;
+    uint8_t* term;
+    uint8_t* trunc;
+    int32_t* info;
+    double* ep_ret;
+    int32_t* ep_len;
+} FmeHostOut;
+/* fme_step, and each env slice's outputs copied into pinned host memory as soon as that slice's kernels are
+ * done, so the copies overlap the later slices' work. Replaces fm_step_async + fm_step_wait's host-buffer
+ * outputs (csrc/fastmario.cpp:611-617) for callers that want host arrays. Async: synchronise the stream before
+ * reading `out`. */
+int fme_step_to_host(FmeEnv* env, const int64_t* d_actions, const FmeHostOut* out, void* stream);
+
 /* OR of the device status bits of all envs since create (call after synchronising). */
 int fme_poll_error(FmeEnv* env, uint32_t* status);
 

@@ -137,8 +137,12 @@ __device__ __forceinline__ AgentCfg agent_cfg(const StepParams& P) {
     return g;
 }
 
-__global__ void __launch_bounds__(32) k_step(StepParams P) {
+// kStep: the timed step (MODE_STEP, frames drawn by k_render) — compiled without the reset-cache builder's
+// branches and the fused renderer, which only MODE_NOOP (construction) uses.
+template <bool kStep>
+__global__ void __launch_bounds__(32, 1) k_step(StepParams P) {
     extern __shared__ __align__(16) uint8_t sm[];
+    if (kStep) P.mode = MODE_STEP;
     const int lane = threadIdx.x, g = blockIdx.x + P.group_base, e = g * 32 + lane;
     const Dev& d = P.d;
     const bool active = e < d.n;
@@ -245,7 +249,7 @@ __global__ void __launch_bounds__(32) k_step(StepParams P) {
 
     const uint32_t summary = (active ? 1u : 0u) | (pooled ? 2u : 0u) | ((uint32_t)cur_slot << 2) | (ended ? 8u : 0u);
     const int K = P.frame_stack;
-    if (P.jobs) {
+    if (kStep) {
         // ---- the frames are drawn by k_render: shift the stacks (and stage the finished episodes' stacks and
         // the reset frames) so that it only has to write frame K-1 of obs or final_obs
         if (active) P.jobs[e] = summary;
@@ -589,7 +593,8 @@ int ensure_constants(int device) {
     CK(cudaMemcpyToSymbol(c_dtab, dt, sizeof(dt)));
     CK(cudaMemcpyToSymbol(c_area, &T, sizeof(T)));
     const int smem = SLAB_BYTES;
-    CK(cudaFuncSetAttribute(k_step, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    CK(cudaFuncSetAttribute(k_step<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    CK(cudaFuncSetAttribute(k_step<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, STEP_SMEM));
     CK(cudaFuncSetAttribute(k_boot, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
     CK(cudaFuncSetAttribute(k_raw, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
     CK(cudaFuncSetAttribute(k_resize, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
@@ -876,7 +881,7 @@ static int create_impl(const FmeConfig* cfg, const uint8_t* rom, int64_t rom_len
             P.out_img = v->d_cache_img; P.out_obs = v->d_cache_obs; P.out_meta = v->d_cache_meta;
             for (int j = 1; j <= C.noop_max; j++) {
                 P.noop_j = j;
-                k_step<<<(nl + 31) / 32, 32, SLAB_BYTES>>>(P);
+                k_step<false><<<(nl + 31) / 32, 32, SLAB_BYTES>>>(P);
                 CK(cudaGetLastError());
             }
             CK(cudaDeviceSynchronize());
@@ -962,7 +967,7 @@ static int launch_step_like(FmeEnv* v, const int64_t* d_actions, void* stream, b
             const int e0 = g0 * 32, e1 = g1 * 32 < v->n ? g1 * 32 : v->n;
             CK(cudaStreamWaitEvent(v->s_emu[c], v->ev_in, 0));
             P.group_base = g0;
-            k_step<<<g1 - g0, 32, STEP_SMEM, v->s_emu[c]>>>(P);
+            k_step<true><<<g1 - g0, 32, STEP_SMEM, v->s_emu[c]>>>(P);
             CK(cudaEventRecord(v->ev_emu[c], v->s_emu[c]));
             CK(cudaStreamWaitEvent(v->s_rnd[c], v->ev_emu[c], 0));
             R.env_base = e0;

@@ -825,6 +825,35 @@ struct Core {
     }
 
     // ================================================================ sprite-0 busy-wait
+    // Last PPU call count up to which the sprite-0 flag keeps its current value while no register is written:
+    // the flag is set only by a pixel test on a line whose sprite list holds sprite 0 (`dots`) and cleared at
+    // dot 1 of the pre-render line. Conservative: never later than the true value, ppu_calls when unsure.
+    FME_HD int32_t s0_steady_until() const {
+        const int32_t FAR = 0x3fffffff;
+        const int c = (int)pcyc;
+        if (s0hit) {
+            if (pstate == PS_VBLANK && scanline >= 241 && scanline <= 260 && c >= 1 && c <= 341)
+                return ppu_calls + (20 * 341 - (((int)scanline - 241) * 341 + (c - 1)));  // to the pre-render line
+            if (pstate == PS_RENDER || pstate == PS_POST) return FAR;  // the clear comes after the next vblank
+            return ppu_calls;
+        }
+        if (!show_bg || !show_spr) return FAR;                        // no pixel test runs
+        if (s0_in_list()) return ppu_calls;                           // the current / next line may test
+        if (oam_addr >= 4) return FAR;                                // later lists start past sprite 0
+        const int range = long_spr ? 16 : 8;
+        const int y_first = (int)OAM(0) + 1, y_last = (int)OAM(0) + range;   // lines whose list (line-1) holds it
+        if (pstate == PS_RENDER && c >= 1 && c <= 341) {
+            const int y = (int)scanline + 1 > y_first ? (int)scanline + 1 : y_first;
+            if (y > y_last || y > 239) return FAR;
+            return ppu_calls + (y - (int)scanline) * 341 - (c - 1);  // dot 1 of line y not yet processed
+        }
+        if (pstate == PS_PRE && c >= 1 && c <= 341) {
+            const int y = y_first > 1 ? y_first : 1;                  // line 0 uses the state checked above
+            if (y > y_last || y > 239) return FAR;
+            return ppu_calls + (341 - c) + y * 341;                   // shortest (odd-frame) pre-render line
+        }
+        return ppu_calls;
+    }
     // The instruction at pc (executing at iteration J) may open a loop that polls $2002 until bit 6 (the
     // sprite-0 flag) changes: `BIT $2002 / BVC|BVS *-3` or `LDA $2002 / AND #$40 / BEQ|BNE *-5`. Once vblank
     // is clear and the address latch reset, another read of $2002 only catches the PPU up, and the loop's
@@ -853,6 +882,17 @@ struct Core {
         }
         it += (int32_t)d_cycles(FME_DTAB(br)) + 1 + ((((br_pc + 2u) ^ pc) & 0xff00u) ? 2 : 0);  // taken branch
         int32_t D = 0;
+        if (s0hit != exit_bit) {
+            // reads whose catch-up target stays within the flag's steady span see the waiting value: skip them
+            // without catching up (a later catch-up reaches the same state); keep a line of margin to the NMI
+            // pre-sync, whose threshold is only refreshed by a catch-up
+            const int32_t S = s0_steady_until();
+            for (;;) {
+                const int32_t Jk = J + D, Jn = Jk + it;
+                if (3 * (Jn + 1) + 2 * 341 >= nmi_thresh || Jn >= FRAME_ITERS || 3 * (Jk + 1) > S) break;
+                D += it;
+            }
+        }
         for (;;) {
             const int32_t Jk = J + D, Jn = Jk + it;
             if (3 * (Jn + 1) >= nmi_thresh || Jn >= FRAME_ITERS) break;

@@ -98,6 +98,9 @@ CONFIGS = {
     "skip1_stack1_pool": dict(levels=["7-4"] * 8, n=8, kw=dict(skip=1, frame_stack=1, maxpool=True, sticky=0.5)),
     "skip6_divergent": dict(levels=["1-1", "6-3"] * 20, n=40, kw=dict(skip=6, sticky=0.25, noop_max=30, maxpool=True),
                             div=True),
+    # 5 groups of 32 (the last ragged) in 4 step slices of uneven size
+    "sliced_150": dict(levels=["1-1", "3-2", "5-4", "8-1", "2-2"] * 30, n=150,
+                       kw=dict(sticky=0.25, noop_max=30, maxpool=True, max_steps=90)),
 }
 
 

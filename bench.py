@@ -36,7 +36,7 @@ UNIT = "env-steps/s"
 #            way), the frame-stack shift (3 x 7056 B read and written), actions and outputs (58 B)
 #   k_render the new 84x84 frame (7056 B) and the job word (the PPU logs it replays are the emulation
 #            kernel's intermediate output, not counted)
-ALGO_BYTES = {"k_step": 2 * (2336 + 2048) + 2 * 37 * 4 + 2 * 3 * 7056 + 58, "k_render": 7056 + 4}
+ALGO_BYTES = {"k_step": 2 * (2336 + 2048) + 2 * 37 * 4 + 58 + 4, "k_render": 2 * 3 * 7056 + 7056 + 4}
 
 
 def load_package():

@@ -250,26 +250,9 @@ __global__ void __launch_bounds__(32, 1) k_step(StepParams P) {
     const uint32_t summary = (active ? 1u : 0u) | (pooled ? 2u : 0u) | ((uint32_t)cur_slot << 2) | (ended ? 8u : 0u);
     const int K = P.frame_stack;
     if (kStep) {
-        // ---- the frames are drawn by k_render: shift the stacks (and stage the finished episodes' stacks and
-        // the reset frames) so that it only has to write frame K-1 of obs or final_obs
-        if (active) P.jobs[e] = summary;
-        for (int j = 0; j < 32; j++) {
-            const uint32_t sj = __shfl_sync(FULL, summary, j);
-            const int cij = __shfl_sync(FULL, reset_ci, j);
-            if (!(sj & 1u)) continue;
-            const int ej = g * 32 + j;
-            uint8_t* o = P.obs + (size_t)ej * K * OBS_BYTES;
-            if (K > 1) wmove16(o, o + OBS_BYTES, (K - 1) * OBS_BYTES, lane);
-            __syncwarp();
-            if (sj & 8u) {
-                uint8_t* f = P.fin + (size_t)ej * K * OBS_BYTES;
-                if (K > 1) wcopy16(f, o, (K - 1) * OBS_BYTES, lane);
-                __syncwarp();
-                if (K > 1) wzero16(o, (K - 1) * OBS_BYTES, lane);
-                wcopy16(o + (size_t)(K - 1) * OBS_BYTES, P.cache.obs + (size_t)cij * OBS_BYTES, OBS_BYTES, lane);
-            }
-            __syncwarp();
-        }
+        // ---- k_render draws the frame, shifts the stack and stages finished episodes (job word: summary bits,
+        // reset-cache entry above them)
+        if (active) P.jobs[e] = summary | ((uint32_t)reset_ci << 4);
         return;
     }
 
@@ -337,11 +320,43 @@ static_assert(RB_VRAM % 16 == 0 && RB_OAM % 16 == 0 && RB_LUT % 16 == 0 && RB_OB
 
 struct RenderParams {
     Dev d;
-    const uint32_t* jobs;
+    const uint32_t* jobs;   // per env: 1 active | 2 max-pooled | 4 slot of the last frame | 8 ended | reset entry << 4
     uint8_t* obs; uint8_t* fin;
+    const uint8_t* cache_obs;   // reset-cache observations (entry x 7056)
     int frame_stack;
     int env_base;   // first env of this launch
 };
+
+// The frame-stack update of one band (BAND_OUT rows of every 84x84 frame, 441 words at the same offset in
+// each): frames 1..K-1 move down to 0..K-2 — into the final stack when the episode ended, whose live stack
+// then restarts as K-1 zero frames and the reset observation. Frame K-1 (the new frame) is written by the
+// caller. Each lane keeps its share of a frame in registers between the loads and the stores.
+constexpr int BAND_WORDS = BAND_OUT * OBS / 4, FRAME_WORDS = OBS_BYTES / 4, BAND_PER_LANE = (BAND_WORDS + 31) / 32;
+static_assert(BAND_OUT * OBS % 4 == 0, "bands are whole words");
+__device__ __forceinline__ void stack_band(uint32_t* o, uint32_t* f, const uint32_t* reset_obs, int K, int lane) {
+    uint32_t* dst = f ? f : o;
+    for (int j = 0; j + 1 < K; j++) {
+        uint32_t v[BAND_PER_LANE];
+#pragma unroll
+        for (int q = 0; q < BAND_PER_LANE; q++) {
+            const int i = lane + 32 * q;
+            if (i < BAND_WORDS) v[q] = o[(j + 1) * FRAME_WORDS + i];
+        }
+        __syncwarp();
+#pragma unroll
+        for (int q = 0; q < BAND_PER_LANE; q++) {
+            const int i = lane + 32 * q;
+            if (i < BAND_WORDS) dst[j * FRAME_WORDS + i] = v[q];
+        }
+    }
+    if (f) {
+        __syncwarp();
+        for (int j = 0; j + 1 < K; j++)
+            for (int i = lane; i < BAND_WORDS; i += 32) o[j * FRAME_WORDS + i] = 0u;
+        for (int i = lane; i < BAND_WORDS; i += 32) o[(K - 1) * FRAME_WORDS + i] = reset_obs[i];
+    }
+    __syncwarp();
+}
 __global__ void __launch_bounds__(32) k_render(RenderParams P) {
     extern __shared__ __align__(16) uint8_t sm[];
     const int lane = threadIdx.x;
@@ -356,6 +371,11 @@ __global__ void __launch_bounds__(32) k_render(RenderParams P) {
     L.row_lo = band * BAND_ROWS; L.row_hi = L.row_lo + BAND_ROWS;
     if (lane < 16) reinterpret_cast<uint4*>(sm + RB_LUT)[lane] = reinterpret_cast<const uint4*>(d.lut)[lane];
     __syncwarp();
+    const int K = P.frame_stack;
+    const size_t band_off = (size_t)band * BAND_OUT * OBS;
+    stack_band(reinterpret_cast<uint32_t*>(P.obs + (size_t)e * K * OBS_BYTES + band_off),
+               (job & 8u) ? reinterpret_cast<uint32_t*>(P.fin + (size_t)e * K * OBS_BYTES + band_off) : nullptr,
+               reinterpret_cast<const uint32_t*>(P.cache_obs + (size_t)(job >> 4) * OBS_BYTES + band_off), K, lane);
     const int cs = (int)((job >> 2) & 1u);
     const int cap = d.log_cap;
     if (job & 2u) {
@@ -365,8 +385,7 @@ __global__ void __launch_bounds__(32) k_render(RenderParams P) {
         render_slot(d.logs + slot_off(e, cs, cap), L, d, false, false, lane);
     }
     resize_band(L.fb, L.row_lo, band * BAND_OUT, band * BAND_OUT + BAND_OUT, sm + RB_OBS, lane);
-    const int K = P.frame_stack;
-    uint8_t* dst = ((job & 8u) ? P.fin : P.obs) + ((size_t)e * K + (K - 1)) * OBS_BYTES + (size_t)band * BAND_OUT * OBS;
+    uint8_t* dst = ((job & 8u) ? P.fin : P.obs) + ((size_t)e * K + (K - 1)) * OBS_BYTES + band_off;
     const uint32_t* src = reinterpret_cast<const uint32_t*>(sm + RB_OBS);
     for (int i = lane; i < BAND_OUT * OBS / 4; i += 32) reinterpret_cast<uint32_t*>(dst)[i] = src[i];
 }
@@ -960,7 +979,7 @@ static int launch_step_like(FmeEnv* v, const int64_t* d_actions, void* stream, b
     } else {
         P.jobs = v->d_jobs;
         RenderParams R;
-        R.d = d; R.jobs = v->d_jobs; R.obs = P.obs; R.fin = P.fin; R.frame_stack = P.frame_stack;
+        R.d = d; R.jobs = v->d_jobs; R.obs = P.obs; R.fin = P.fin; R.cache_obs = P.cache.obs; R.frame_stack = P.frame_stack;
         CK(cudaEventRecord(v->ev_in, s));
         for (int c = 0; c < v->nch; c++) {
             const int g0 = groups * c / v->nch, g1 = groups * (c + 1) / v->nch;

@@ -606,6 +606,10 @@ int ensure_constants(int device) {
     build_dtab(dt);
     AreaTabs T;
     if (!build_area(T)) return fail(FME_E_ARG, "area table has more than 6 taps");
+    for (int dx = 0; dx < OBS; dx++)  // resize_band keeps AREA_XTAPS consecutive column taps in registers
+        for (int k = 1; k < 6; k++)
+            if (T.xw[k][dx] != 0.f && (k >= AREA_XTAPS || T.xs[k][dx] != T.xs[0][dx] + k))
+                return fail(FME_E_ARG, "area column taps are not consecutive");
     for (int dy = 0; dy < OBS; dy++)  // k_render: every tap of an output row lies in that row's band
         for (int m = 0; m < 6 && T.yw[m][dy] != 0.f; m++)
             if (T.ys[m][dy] / BAND_ROWS != dy / BAND_OUT) return fail(FME_E_ARG, "area taps cross a render band");

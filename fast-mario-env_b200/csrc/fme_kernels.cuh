@@ -146,7 +146,8 @@ __device__ void render_slot(const uint8_t* slot, const RLayout& L, const Dev& d,
     uint8_t* fb = L.fb - L.row_lo * SCREEN_W;  // indexed by screen row
     RState rs;
     rs.vram = L.vram; rs.pal = L.pal; rs.oam = L.oam; rs.chr = d.chr;
-    for (int i = 0; i < 4; i++) rs.nt[i] = d.nt[i];
+    rs.ntm = 0;
+    for (int i = 0; i < 4; i++) rs.ntm |= (d.nt[i] >> 10 & 1u) << i;
     uint8_t* stage = L.stage;
     const uint8_t* lut = L.lut;
     {
@@ -304,16 +305,16 @@ __device__ void render_slot(const uint8_t* slot, const RLayout& L, const Dev& d,
 // columns lane, lane+32, lane+64.
 __device__ void resize_band(const uint8_t* fb, int row_lo, int dy_lo, int dy_hi, uint8_t* out, int lane) {
     fb -= row_lo * SCREEN_W;
-    int32_t xs[3][6];
-    float xw[3][6];
+    // a column's taps are AREA_XTAPS consecutive source dots from xs0 (zero-weight padded; checked when the
+    // table is built), so the lane's three columns fit in registers
+    int32_t xs0[3];
+    float xw[3][AREA_XTAPS];
 #pragma unroll
     for (int q = 0; q < 3; q++) {
         int dx = lane + 32 * q;
+        xs0[q] = dx < OBS ? c_area.xs[0][dx] : 0;
 #pragma unroll
-        for (int k = 0; k < 6; k++) {
-            xs[q][k] = dx < OBS ? c_area.xs[k][dx] : 0;
-            xw[q][k] = dx < OBS ? c_area.xw[k][dx] : 0.f;
-        }
+        for (int k = 0; k < AREA_XTAPS; k++) xw[q][k] = dx < OBS ? c_area.xw[k][dx] : 0.f;
     }
     for (int dy = dy_lo; dy < dy_hi; dy++) {
         float sacc[3] = {0.f, 0.f, 0.f};
@@ -325,8 +326,8 @@ __device__ void resize_band(const uint8_t* fb, int row_lo, int dy_lo, int dy_hi,
             for (int q = 0; q < 3; q++) {
                 float b = 0.f;
 #pragma unroll
-                for (int k = 0; k < 6; k++) {
-                    if (xw[q][k] != 0.f) b = fadd(b, fmul((float)row[xs[q][k]], xw[q][k]));
+                for (int k = 0; k < AREA_XTAPS; k++) {
+                    if (xw[q][k] != 0.f) b = fadd(b, fmul((float)row[xs0[q] + k], xw[q][k]));
                 }
                 sacc[q] = fadd(sacc[q], fmul(wy, b));
             }

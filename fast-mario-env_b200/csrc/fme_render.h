@@ -28,6 +28,7 @@
 
 namespace fme {
 
+constexpr int AREA_XTAPS = 4;  // 256 -> 84 columns: at most 4 taps each, consecutive source dots
 struct AreaTabs {           // per output column / row up to 6 (index, weight) taps, zero-weight padded
     int32_t xs[6][OBS];
     float xw[6][OBS];
@@ -41,16 +42,17 @@ struct RState {
     uint8_t* pal;    // 32
     uint8_t* oam;    // 256
     const uint8_t* chr;
-    uint32_t nt[4];
+    uint32_t ntm;    // nametable t maps to VRAM offset ((ntm >> t) & 1) * 0x400 (a bit mask, so it stays in a register)
     // current explicit list (used by segments without a pending evaluation)
     uint32_t nsl, sl_lo, sl_hi;
 };
+FME_HD uint32_t nt_base(uint32_t ntm, uint32_t t) { return ((ntm >> t) & 1u) << 10; }
 
 FME_HD uint32_t r_pb_read(const RState& s, uint32_t addr) {
     if (addr < 0x2000) return FME_LDG(s.chr + addr);
     if (addr < 0x3eff) {
         uint32_t tsel = addr < 0x2400 ? 0u : addr < 0x2800 ? 1u : addr < 0x2c00 ? 2u : 3u;
-        return s.vram[s.nt[tsel] + (addr & 0x3ffu)];
+        return s.vram[nt_base(s.ntm, tsel) + (addr & 0x3ffu)];
     }
     if (addr < 0x3fff) return s.pal[addr & 0x1fu];
     return 0;
@@ -172,13 +174,13 @@ FME_HD uint32_t seg_dot_pa(const RState& s, const Seg& g, int xx, uint32_t nsl, 
     if (g.flags & RF_SHOW_BG) {
         uint32_t vx = v_after(g.v, inc_count_fx(g.fine_x, g.x0, xx));
         uint32_t xf = (g.fine_x + (uint32_t)xx) & 7u;
-        uint32_t tile = s.vram[s.nt[((0x2000u | (vx & 0x0fffu)) >> 10) & 3u] + (vx & 0x3ffu)];
+        uint32_t tile = s.vram[nt_base(s.ntm, ((0x2000u | (vx & 0x0fffu)) >> 10) & 3u) + (vx & 0x3ffu)];
         uint32_t addr = (((tile * 16u) + ((vx >> 12) & 7u)) | ((g.flags & RF_BG_PAGE) ? 0x1000u : 0u)) & 0xffffu;
         uint32_t b = (FME_LDG(s.chr + (addr & 0x1fffu)) >> (7u ^ xf)) & 1u;
         b |= ((FME_LDG(s.chr + ((addr + 8u) & 0x1fffu)) >> (7u ^ xf)) & 1u) << 1;
         if (b) {
             uint32_t aaddr = 0x23C0u | (vx & 0x0C00u) | ((vx >> 4) & 0x38u) | ((vx >> 2) & 0x07u);
-            uint32_t attr = s.vram[s.nt[(aaddr >> 10) & 3u] + (aaddr & 0x3ffu)];
+            uint32_t attr = s.vram[nt_base(s.ntm, (aaddr >> 10) & 3u) + (aaddr & 0x3ffu)];
             uint32_t shift = ((vx >> 4) & 4u) | (vx & 2u);
             pa = b | (((attr >> shift) & 3u) << 2);
         }
@@ -282,12 +284,12 @@ FME_HD uint32_t sprite_info(const RState& rs, int i) {
 
 // background tile of v: pattern bytes (MSB = leftmost dot) and the 2 palette-select bits (nes_core.hpp:453-464)
 FME_HD void bg_tile(const RState& rs, uint32_t v, uint32_t bg_page, uint32_t& lo, uint32_t& hi, uint32_t& at) {
-    uint32_t tile = rs.vram[rs.nt[(v >> 10) & 3u] + (v & 0x3ffu)];
+    uint32_t tile = rs.vram[nt_base(rs.ntm, (v >> 10) & 3u) + (v & 0x3ffu)];
     uint32_t addr = ((tile * 16u) + ((v >> 12) & 7u)) | (bg_page << 12);
     lo = FME_LDG(rs.chr + (addr & 0x1fffu));
     hi = FME_LDG(rs.chr + ((addr + 8u) & 0x1fffu));
     uint32_t aaddr = 0x23C0u | (v & 0x0C00u) | ((v >> 4) & 0x38u) | ((v >> 2) & 0x07u);
-    uint32_t attr = rs.vram[rs.nt[(aaddr >> 10) & 3u] + (aaddr & 0x3ffu)];
+    uint32_t attr = rs.vram[nt_base(rs.ntm, (aaddr >> 10) & 3u) + (aaddr & 0x3ffu)];
     at = (attr >> (((v >> 4) & 4u) | (v & 2u))) & 3u;
 }
 

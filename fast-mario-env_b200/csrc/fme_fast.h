@@ -114,91 +114,93 @@ struct Fast {
         int cls = 3;  // 0 read m, 1 store to loc, 2 read-modify-write loc, 3 done
         uint32_t m = 0;
         switch (hid) {
-            case H_RD_IMM: m = w; cls = 0; break;
-            case H_RD_ZP: m = R(w); cls = 0; break;
+#define FME_X_RD(OP)                                                                          \
+            case H_X_RD + OP: alu_read(h, OP, w); h.pc = npc; return skip;                    \
+            case H_X_RD + 16 + OP: alu_read(h, OP, R(w)); h.pc = npc; return skip;
+            FME_X_RD(R_ORA) FME_X_RD(R_AND) FME_X_RD(R_EOR) FME_X_RD(R_ADC) FME_X_RD(R_LDA) FME_X_RD(R_CMP)
+            FME_X_RD(R_SBC) FME_X_RD(R_BIT) FME_X_RD(R_LDX) FME_X_RD(R_LDY) FME_X_RD(R_CPX) FME_X_RD(R_CPY)
+#undef FME_X_RD
+            case H_X_ST + W_STA: W(w, h.a); h.pc = npc; return skip;
+            case H_X_ST + W_STX: W(w, h.x); h.pc = npc; return skip;
+            case H_X_ST + W_STY: W(w, h.y); h.pc = npc; return skip;
+#define FME_X_RMW(OP)                                                                         \
+            case H_X_RMW + OP: W(w, alu_rmw(h, OP, R(w))); h.pc = npc; return skip;           \
+            case H_X_ACC + OP: h.a = alu_rmw(h, OP, h.a); h.pc = npc; return skip;
+            FME_X_RMW(X_ASL) FME_X_RMW(X_ROL) FME_X_RMW(X_LSR) FME_X_RMW(X_ROR) FME_X_RMW(X_DEC) FME_X_RMW(X_INC)
+#undef FME_X_RMW
+            case H_X_IMPL + I_BRK: {
+                uint32_t r = npc + 1;  // BRK skips its padding byte
+                W(0x100u | h.sp, (r >> 8) & 0xffu); h.sp = (h.sp - 1) & 0xffu;
+                W(0x100u | h.sp, r & 0xffu); h.sp = (h.sp - 1) & 0xffu;
+                W(0x100u | h.sp, h.p | 0x30u); h.sp = (h.sp - 1) & 0xffu;
+                h.p |= F_I;
+                h.pc = P(0xfffe) | (P(0xffff) << 8);
+                return skip + 7;
+            }
+            case H_X_IMPL + I_PHP: W(0x100u | h.sp, h.p); h.sp = (h.sp - 1) & 0xffu; h.pc = npc; return skip;
+            case H_X_IMPL + I_CLC: setf(h, F_C, false); h.pc = npc; return skip;
+            case H_X_IMPL + I_JSR: {
+                uint32_t r = (npc + 1) & 0x1ffffu;
+                W(0x100u | h.sp, (r >> 8) & 0xffu); h.sp = (h.sp - 1) & 0xffu;
+                W(0x100u | h.sp, r & 0xffu); h.sp = (h.sp - 1) & 0xffu;
+                h.pc = w;
+                return skip;
+            }
+            case H_X_IMPL + I_PLP: h.sp = (h.sp + 1) & 0xffu; h.p = R(0x100u | h.sp); h.pc = npc; return skip;
+            case H_X_IMPL + I_SEC: setf(h, F_C, true); h.pc = npc; return skip;
+            case H_X_IMPL + I_RTI: {
+                h.sp = (h.sp + 1) & 0xffu; h.p = R(0x100u | h.sp);
+                h.sp = (h.sp + 1) & 0xffu; uint32_t lo = R(0x100u | h.sp);
+                h.sp = (h.sp + 1) & 0xffu; h.pc = lo | (R(0x100u | h.sp) << 8);
+                return skip;
+            }
+            case H_X_IMPL + I_PHA: W(0x100u | h.sp, h.a); h.sp = (h.sp - 1) & 0xffu; h.pc = npc; return skip;
+            case H_X_IMPL + I_JMP: h.pc = w; return skip;
+            case H_X_IMPL + I_CLI: setf(h, F_I, false); h.pc = npc; return skip;
+            case H_X_IMPL + I_RTS: {
+                h.sp = (h.sp + 1) & 0xffu; uint32_t lo = R(0x100u | h.sp);
+                h.sp = (h.sp + 1) & 0xffu; h.pc = ((lo | (R(0x100u | h.sp) << 8)) + 1) & 0xffffu;
+                return skip;
+            }
+            case H_X_IMPL + I_PLA: h.sp = (h.sp + 1) & 0xffu; h.a = R(0x100u | h.sp); zn(h, h.a); h.pc = npc; return skip;
+            case H_X_IMPL + I_JMPI: {  // the builder routed I/O pointer addresses to the exact path
+                const uint32_t hiad = (w & 0xff00u) | ((w + 1) & 0xffu);
+                h.pc = M(w) | (M(hiad) << 8);
+                return skip;
+            }
+            case H_X_IMPL + I_SEI: setf(h, F_I, true); h.pc = npc; return skip;
+            case H_X_IMPL + I_DEY: h.y = (h.y - 1) & 0xffu; zn(h, h.y); h.pc = npc; return skip;
+            case H_X_IMPL + I_TXA: h.a = h.x; zn(h, h.a); h.pc = npc; return skip;
+            case H_X_IMPL + I_TYA: h.a = h.y; zn(h, h.a); h.pc = npc; return skip;
+            case H_X_IMPL + I_TXS: h.sp = h.x; h.pc = npc; return skip;
+            case H_X_IMPL + I_TAY: h.y = h.a; zn(h, h.y); h.pc = npc; return skip;
+            case H_X_IMPL + I_TAX: h.x = h.a; zn(h, h.x); h.pc = npc; return skip;
+            case H_X_IMPL + I_CLV: setf(h, F_V, false); h.pc = npc; return skip;
+            case H_X_IMPL + I_TSX: h.x = h.sp; zn(h, h.x); h.pc = npc; return skip;
+            case H_X_IMPL + I_INY: h.y = (h.y + 1) & 0xffu; zn(h, h.y); h.pc = npc; return skip;
+            case H_X_IMPL + I_DEX: h.x = (h.x - 1) & 0xffu; zn(h, h.x); h.pc = npc; return skip;
+            case H_X_IMPL + I_CLD: setf(h, F_D, false); h.pc = npc; return skip;
+            case H_X_IMPL + I_INX: h.x = (h.x + 1) & 0xffu; zn(h, h.x); h.pc = npc; return skip;
+            case H_X_IMPL + I_NOP: h.pc = npc; return skip;
+            case H_X_IMPL + I_SED: setf(h, F_D, true); h.pc = npc; return skip;
+            // indexed and indirect forms: address first (I/O check below), then the operation
             case H_RD_ZPX: m = R((w + h.x) & 0xffu); cls = 0; break;
             case H_RD_ZPY: m = R((w + h.y) & 0xffu); cls = 0; break;
-            case H_RD_ABS: m = R(w); cls = 0; break;
             case H_RD_ABSX: base = w; loc = (w + h.x) & 0xffffu; cls = 4; break;
             case H_RD_ABSY: base = w; loc = (w + h.y) & 0xffffu; cls = 4; break;
             case H_RD_INDX: { const uint32_t za = (h.x + w) & 0xffu; loc = R(za) | (R((za + 1) & 0xffu) << 8); cls = 4; break; }
             case H_RD_INDY: base = R(w) | (R((w + 1) & 0xffu) << 8); loc = (base + h.y) & 0xffffu; cls = 4; break;
-            case H_ST_ZP: loc = w; cls = 1; break;
             case H_ST_ZPX: loc = (w + h.x) & 0xffu; cls = 1; break;
             case H_ST_ZPY: loc = (w + h.y) & 0xffu; cls = 1; break;
-            case H_ST_ABS: loc = w; cls = 1; break;
             case H_ST_ABSX: base = w; loc = (w + h.x) & 0xffffu; cls = 5; break;
             case H_ST_ABSY: base = w; loc = (w + h.y) & 0xffffu; cls = 5; break;
             case H_ST_INDX: { const uint32_t za = (h.x + w) & 0xffu; loc = R(za) | (R((za + 1) & 0xffu) << 8); cls = 5; break; }
             case H_ST_INDY: base = R(w) | (R((w + 1) & 0xffu) << 8); loc = (base + h.y) & 0xffffu; cls = 5; break;
             case H_NOPW: break;
-            case H_RMW_ZP: loc = w; cls = 2; break;
             case H_RMW_ZPX: loc = (w + h.x) & 0xffu; cls = 2; break;
-            case H_RMW_ABS: loc = w; cls = 2; break;
             case H_RMW_ABSX: base = w; loc = (w + h.x) & 0xffffu; cls = 6; break;
-            case H_ACC: h.a = alu_rmw(h, op, h.a); break;
             case H_BRANCH:
                 if (((h.p >> (op & 7u)) & 1u) == ((op >> 3) & 1u)) { skip += (int32_t)(h.uy >> 24); npc = w; }
-                break;
-            case H_IMPL:
-                switch (op) {
-                    case I_BRK: {
-                        uint32_t r = npc + 1;  // BRK skips its padding byte
-                        W(0x100u | h.sp, (r >> 8) & 0xffu); h.sp = (h.sp - 1) & 0xffu;
-                        W(0x100u | h.sp, r & 0xffu); h.sp = (h.sp - 1) & 0xffu;
-                        W(0x100u | h.sp, h.p | 0x30u); h.sp = (h.sp - 1) & 0xffu;
-                        h.p |= F_I;
-                        npc = P(0xfffe) | (P(0xffff) << 8);
-                        skip += 7;
-                        break;
-                    }
-                    case I_PHP: W(0x100u | h.sp, h.p); h.sp = (h.sp - 1) & 0xffu; break;
-                    case I_CLC: setf(h, F_C, false); break;
-                    case I_JSR: {
-                        uint32_t r = (npc + 1) & 0x1ffffu;
-                        W(0x100u | h.sp, (r >> 8) & 0xffu); h.sp = (h.sp - 1) & 0xffu;
-                        W(0x100u | h.sp, r & 0xffu); h.sp = (h.sp - 1) & 0xffu;
-                        npc = w;
-                        break;
-                    }
-                    case I_PLP: h.sp = (h.sp + 1) & 0xffu; h.p = R(0x100u | h.sp); break;
-                    case I_SEC: setf(h, F_C, true); break;
-                    case I_RTI: {
-                        h.sp = (h.sp + 1) & 0xffu; h.p = R(0x100u | h.sp);
-                        h.sp = (h.sp + 1) & 0xffu; uint32_t lo = R(0x100u | h.sp);
-                        h.sp = (h.sp + 1) & 0xffu; npc = lo | (R(0x100u | h.sp) << 8);
-                        break;
-                    }
-                    case I_PHA: W(0x100u | h.sp, h.a); h.sp = (h.sp - 1) & 0xffu; break;
-                    case I_JMP: npc = w; break;
-                    case I_CLI: setf(h, F_I, false); break;
-                    case I_RTS: {
-                        h.sp = (h.sp + 1) & 0xffu; uint32_t lo = R(0x100u | h.sp);
-                        h.sp = (h.sp + 1) & 0xffu; npc = ((lo | (R(0x100u | h.sp) << 8)) + 1) & 0xffffu;
-                        break;
-                    }
-                    case I_PLA: h.sp = (h.sp + 1) & 0xffu; h.a = R(0x100u | h.sp); zn(h, h.a); break;
-                    case I_JMPI: {  // the builder routed I/O pointer addresses to the exact path
-                        const uint32_t hiad = (w & 0xff00u) | ((w + 1) & 0xffu);
-                        npc = M(w) | (M(hiad) << 8);
-                        break;
-                    }
-                    case I_SEI: setf(h, F_I, true); break;
-                    case I_DEY: h.y = (h.y - 1) & 0xffu; zn(h, h.y); break;
-                    case I_TXA: h.a = h.x; zn(h, h.a); break;
-                    case I_TYA: h.a = h.y; zn(h, h.a); break;
-                    case I_TXS: h.sp = h.x; break;
-                    case I_TAY: h.y = h.a; zn(h, h.y); break;
-                    case I_TAX: h.x = h.a; zn(h, h.x); break;
-                    case I_CLV: setf(h, F_V, false); break;
-                    case I_TSX: h.x = h.sp; zn(h, h.x); break;
-                    case I_INY: h.y = (h.y + 1) & 0xffu; zn(h, h.y); break;
-                    case I_DEX: h.x = (h.x - 1) & 0xffu; zn(h, h.x); break;
-                    case I_CLD: setf(h, F_D, false); break;
-                    case I_INX: h.x = (h.x + 1) & 0xffu; zn(h, h.x); break;
-                    case I_NOP: break;
-                    default: setf(h, F_D, true); break;  // SED
-                }
                 break;
             case H_BAD_ABSX:
                 if (((w + h.x) ^ w) & 0xff00u) skip += 1;

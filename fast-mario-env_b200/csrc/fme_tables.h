@@ -217,6 +217,15 @@ inline void build_uops(const uint8_t* prg, const uint32_t* dtab, uint32_t* out /
             }
         }
         if (hid == H_SLOW) { len = 0; w = w16; }  // operand kept for diagnostics only
+        switch (hid) {  // the forms whose operation is folded into the handler id
+            case H_RD_IMM: hid = H_X_RD + op; break;
+            case H_RD_ZP: case H_RD_ABS: hid = H_X_RD + 16 + op; break;
+            case H_ST_ZP: case H_ST_ABS: hid = H_X_ST + op; break;
+            case H_RMW_ZP: case H_RMW_ABS: hid = H_X_RMW + op; break;
+            case H_ACC: hid = H_X_ACC + op; break;
+            case H_IMPL: hid = H_X_IMPL + op; break;
+            default: break;
+        }
         out[2 * (a - 0x8000u)] = hid | (opc << 8) | (op << 16) | (pen << 21) | (len << 22) | ((idle ? 1u : 0u) << 24);
         out[2 * (a - 0x8000u) + 1] = (w & 0xffffu) | (cyc << 16) | (extra << 24);
     }

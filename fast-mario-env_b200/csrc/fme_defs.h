@@ -84,6 +84,11 @@ enum Hid : uint32_t {
     H_X_RMW = 72,       // + op: read-modify-write of a static RAM address
     H_X_ACC = 80,       // + op: accumulator shifts / rotates
     H_X_IMPL = 96,      // + op: implied, stack and jump instructions
+    H_X_RDZX = 128,     // + op: read (zp,X)            the indexed reads below check the computed address
+    H_X_RDAX = 144,     // + op: read abs,X             for I/O (exact path) and add the page-cross cycle
+    H_X_RDAY = 160,     // + op: read abs,Y
+    H_X_RDIY = 176,     // + op: read (zp),Y
+    H_X_RDIX = 192,     // + op: read (zp,X)
 };
 constexpr uint32_t UOP_IDLE = 1u << 24;
 constexpr int UOP_WORDS = 2 * 0x8000;

@@ -120,6 +120,35 @@ struct Fast {
             FME_X_RD(R_ORA) FME_X_RD(R_AND) FME_X_RD(R_EOR) FME_X_RD(R_ADC) FME_X_RD(R_LDA) FME_X_RD(R_CMP)
             FME_X_RD(R_SBC) FME_X_RD(R_BIT) FME_X_RD(R_LDX) FME_X_RD(R_LDY) FME_X_RD(R_CPX) FME_X_RD(R_CPY)
 #undef FME_X_RD
+#define FME_X_RDI(OP)                                                                                          \
+            case H_X_RDZX + OP: alu_read(h, OP, R((w + h.x) & 0xffu)); h.pc = npc; return skip;                \
+            case H_X_RDAX + OP: {                                                                              \
+                const uint32_t l = (w + h.x) & 0xffffu;                                                        \
+                if (io(l)) return -1;                                                                          \
+                if (pen && ((w ^ l) & 0xff00u)) skip += 1;                                                     \
+                alu_read(h, OP, M(l)); h.pc = npc; return skip;                                                \
+            }                                                                                                  \
+            case H_X_RDAY + OP: {                                                                              \
+                const uint32_t l = (w + h.y) & 0xffffu;                                                        \
+                if (io(l)) return -1;                                                                          \
+                if (pen && ((w ^ l) & 0xff00u)) skip += 1;                                                     \
+                alu_read(h, OP, M(l)); h.pc = npc; return skip;                                                \
+            }                                                                                                  \
+            case H_X_RDIY + OP: {                                                                              \
+                const uint32_t b = R(w) | (R((w + 1) & 0xffu) << 8), l = (b + h.y) & 0xffffu;                  \
+                if (io(l)) return -1;                                                                          \
+                if (pen && ((b ^ l) & 0xff00u)) skip += 1;                                                     \
+                alu_read(h, OP, M(l)); h.pc = npc; return skip;                                                \
+            }                                                                                                  \
+            case H_X_RDIX + OP: {                                                                              \
+                const uint32_t za = (h.x + w) & 0xffu, l = R(za) | (R((za + 1) & 0xffu) << 8);                 \
+                if (io(l)) return -1;                                                                          \
+                if (pen && (l & 0xff00u)) skip += 1;                                                           \
+                alu_read(h, OP, M(l)); h.pc = npc; return skip;                                                \
+            }
+            FME_X_RDI(R_ORA) FME_X_RDI(R_AND) FME_X_RDI(R_EOR) FME_X_RDI(R_ADC) FME_X_RDI(R_LDA) FME_X_RDI(R_CMP)
+            FME_X_RDI(R_SBC) FME_X_RDI(R_BIT) FME_X_RDI(R_LDX) FME_X_RDI(R_LDY) FME_X_RDI(R_CPX) FME_X_RDI(R_CPY)
+#undef FME_X_RDI
             case H_X_ST + W_STA: W(w, h.a); h.pc = npc; return skip;
             case H_X_ST + W_STX: W(w, h.x); h.pc = npc; return skip;
             case H_X_ST + W_STY: W(w, h.y); h.pc = npc; return skip;
@@ -184,12 +213,7 @@ struct Fast {
             case H_X_IMPL + I_NOP: h.pc = npc; return skip;
             case H_X_IMPL + I_SED: setf(h, F_D, true); h.pc = npc; return skip;
             // indexed and indirect forms: address first (I/O check below), then the operation
-            case H_RD_ZPX: m = R((w + h.x) & 0xffu); cls = 0; break;
             case H_RD_ZPY: m = R((w + h.y) & 0xffu); cls = 0; break;
-            case H_RD_ABSX: base = w; loc = (w + h.x) & 0xffffu; cls = 4; break;
-            case H_RD_ABSY: base = w; loc = (w + h.y) & 0xffffu; cls = 4; break;
-            case H_RD_INDX: { const uint32_t za = (h.x + w) & 0xffu; loc = R(za) | (R((za + 1) & 0xffu) << 8); cls = 4; break; }
-            case H_RD_INDY: base = R(w) | (R((w + 1) & 0xffu) << 8); loc = (base + h.y) & 0xffffu; cls = 4; break;
             case H_ST_ZPX: loc = (w + h.x) & 0xffu; cls = 1; break;
             case H_ST_ZPY: loc = (w + h.y) & 0xffu; cls = 1; break;
             case H_ST_ABSX: base = w; loc = (w + h.x) & 0xffffu; cls = 5; break;

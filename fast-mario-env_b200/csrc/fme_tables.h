@@ -217,14 +217,25 @@ inline void build_uops(const uint8_t* prg, const uint32_t* dtab, uint32_t* out /
             }
         }
         if (hid == H_SLOW) { len = 0; w = w16; }  // operand kept for diagnostics only
-        switch (hid) {  // the forms whose operation is folded into the handler id
-            case H_RD_IMM: hid = H_X_RD + op; break;
-            case H_RD_ZP: case H_RD_ABS: hid = H_X_RD + 16 + op; break;
-            case H_ST_ZP: case H_ST_ABS: hid = H_X_ST + op; break;
-            case H_RMW_ZP: case H_RMW_ABS: hid = H_X_RMW + op; break;
-            case H_ACC: hid = H_X_ACC + op; break;
-            case H_IMPL: hid = H_X_IMPL + op; break;
-            default: break;
+        {  // the forms whose operation is folded into the handler id (an operation outside its family's range
+           // would alias another handler: such an instruction takes the exact path)
+            uint32_t base = 0, nops = 0;
+            switch (hid) {
+                case H_RD_IMM: base = H_X_RD; nops = 12; break;
+                case H_RD_ZP: case H_RD_ABS: base = H_X_RD + 16; nops = 12; break;
+                case H_ST_ZP: case H_ST_ABS: base = H_X_ST; nops = 3; break;
+                case H_RMW_ZP: case H_RMW_ABS: base = H_X_RMW; nops = 6; break;
+                case H_ACC: base = H_X_ACC; nops = 6; break;
+                case H_IMPL: base = H_X_IMPL; nops = 28; break;
+                case H_RD_ZPX: base = H_X_RDZX; nops = 12; break;
+                case H_RD_ABSX: base = H_X_RDAX; nops = 12; break;
+                case H_RD_ABSY: base = H_X_RDAY; nops = 12; break;
+                case H_RD_INDY: base = H_X_RDIY; nops = 12; break;
+                case H_RD_INDX: base = H_X_RDIX; nops = 12; break;
+                default: break;
+            }
+            if (nops) hid = op < nops ? base + op : (uint32_t)H_SLOW;
+            if (hid == H_SLOW) { len = 0; w = w16; }
         }
         out[2 * (a - 0x8000u)] = hid | (opc << 8) | (op << 16) | (pen << 21) | (len << 22) | ((idle ? 1u : 0u) << 24);
         out[2 * (a - 0x8000u) + 1] = (w & 0xffffu) | (cyc << 16) | (extra << 24);

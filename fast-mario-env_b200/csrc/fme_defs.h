@@ -78,6 +78,8 @@ enum Hid : uint32_t {
     H_ST_ZP, H_ST_ZPX, H_ST_ZPY, H_ST_ABS, H_ST_ABSX, H_ST_ABSY, H_ST_INDX, H_ST_INDY, H_NOPW,
     H_RMW_ZP, H_RMW_ZPX, H_RMW_ABS, H_RMW_ABSX,
     H_ACC, H_BRANCH, H_IMPL, H_BAD, H_BAD_ABSX,
+    H_JOY_RD, H_JOY_ST,  // abs read of $4016/$4017 (operand = port) / abs store to $4016: controller ports,
+                         // run beside the exact path without the hand-over of the register state
     // specialised forms: the operation is part of the handler id, so one dispatch runs the instruction
     H_X_RD = 32,        // + op: operand value in the micro-op (immediate, ROM); + 16 + op: static RAM address
     H_X_ST = 64,        // + op: store to a static RAM address

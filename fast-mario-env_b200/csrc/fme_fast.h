@@ -226,6 +226,7 @@ struct Fast {
             case H_BRANCH:
                 if (((h.p >> (op & 7u)) & 1u) == ((op >> 3) & 1u)) { skip += (int32_t)(h.uy >> 24); npc = w; }
                 break;
+            case H_JOY_RD: case H_JOY_ST: return -1;  // hot_step's controller path
             case H_BAD_ABSX:
                 if (((w + h.x) ^ w) & 0xff00u) skip += 1;
                 h.bad++;
@@ -268,6 +269,23 @@ FME_HD void hot_in(Hot& h, const Core& c, const Fast& f) {
     fetch(h, f);
 }
 
+// Controller port access (Core::joy_read and the $4016 strobe of Core::wr_io): the only console state it
+// touches is the controller's, which Hot does not hold, so the registers stay in Hot.
+FME_HD int32_t joy_exec(Hot& h, Core& c) {
+    const uint32_t op = (h.ux >> 16) & 31u;
+    if ((h.ux & 0xffu) == H_JOY_RD) {
+        Fast::alu_read(h, op, c.joy_read((int)(h.uy & 1u)));
+    } else {
+        const uint32_t v = op == W_STA ? h.a : op == W_STX ? h.x : h.y;
+        for (int i = 0; i < 2; i++) {
+            c.joy_strobe[i] = v & 1u;
+            if (!c.joy_strobe[i]) c.joy_bits[i] = c.joy_buttons[i];
+        }
+    }
+    h.pc = (h.pc + 3u) & 0xffffu;
+    return (int32_t)((h.uy >> 16) & 0xffu);
+}
+
 // One scheduling unit of the frame loop (the body of nes_core.hpp:1169-1201) on the register state.
 // Returns false when exec_at reached the frame end (the caller then runs Core::end_frame via hot_out).
 FME_HD bool hot_step(Hot& h, Core& c, const Fast& f) {
@@ -300,7 +318,10 @@ FME_HD bool hot_step(Hot& h, Core& c, const Fast& f) {
         }
         S = (h.ux & 0xffu) != H_SLOW ? f.exec(h) : -1;
     }
-    if (S < 0) {
+    if (S < 0 && ((h.ux & 0xffu) == H_JOY_RD || (h.ux & 0xffu) == H_JOY_ST)) {
+        S = joy_exec(h, c);
+        fetch(h, f);
+    } else if (S < 0) {
         const uint32_t opc = h.pc >= 0x8000u ? (h.ux >> 8) & 0xffu : 0x100u;
         hot_out(h, c);
         S = slow_execute(c, J, opc);

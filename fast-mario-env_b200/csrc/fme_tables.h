@@ -159,6 +159,7 @@ inline void build_uops(const uint8_t* prg, const uint32_t* dtab, uint32_t* out /
                         case M_ABS:
                             if (w16 < 0x2000u) { hid = H_RD_ABS; w = w16; }
                             else if (w16 >= 0x8000u) { hid = H_RD_IMM; w = P(w16); }  // ROM operand
+                            else if ((w16 | 1u) == 0x4017u) { hid = H_JOY_RD; w = w16 & 1u; }
                             break;
                         case M_ABSX: hid = H_RD_ABSX; w = w16; break;
                         case M_ABSY: hid = H_RD_ABSY; w = w16; break;
@@ -177,6 +178,7 @@ inline void build_uops(const uint8_t* prg, const uint32_t* dtab, uint32_t* out /
                         case M_ABS:
                             if (w16 < 0x2000u) { hid = H_ST_ABS; w = w16; }
                             else if (w16 >= 0x8000u) hid = H_NOPW;
+                            else if (w16 == 0x4016u) hid = H_JOY_ST;
                             break;
                         case M_ABSX: hid = H_ST_ABSX; w = w16; break;
                         case M_ABSY: hid = H_ST_ABSY; w = w16; break;

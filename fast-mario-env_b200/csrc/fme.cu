@@ -177,10 +177,11 @@ __global__ void __launch_bounds__(32, 1) k_step(StepParams P) {
     if (active) ag.start(c, ev, cfg, act, d.logs + slot_off(e, 0, cap), d.logs + slot_off(e, 1, cap));
     // one emulated instruction per lane per iteration; the vote keeps the warp converged at the loop head
     const Fast fst{c.ram, d.prg, d.uop};
+    const uint32_t ip0 = __ldg(d.uop + UOP_WORDS), ip1 = __ldg(d.uop + UOP_WORDS + 1);
     Hot h;
     hot_in(h, c, fst);
     for (;;) {
-        const uint32_t key = sched_key(running, h);
+        const uint32_t key = sched_key_pc(running, h, ip0, ip1);
         const uint32_t mn = __reduce_min_sync(FULL, key);
         if (mn == 0xffffffffu) break;
         if (key == mn && !hot_step(h, c, fst)) {
@@ -675,14 +676,17 @@ struct DevBufs {  // one set of per-env state buffers
 
 // The PRG image and its micro-op table share one allocation: 32 KB of PRG, then 2 words per PRG address.
 constexpr size_t PRG_UOP_OFF = 0x8000;
-constexpr size_t PRG_ALLOC = PRG_UOP_OFF + (size_t)UOP_WORDS * 4;
+constexpr size_t PRG_ALLOC = PRG_UOP_OFF + (size_t)(UOP_WORDS + 2) * 4;  // + the first two idle-loop PCs
 cudaError_t upload_prg(uint8_t* d_prg, const std::vector<uint8_t>& prg) {
     uint32_t dt[256];
     build_dtab(dt);
-    std::vector<uint32_t> uops(UOP_WORDS);
+    std::vector<uint32_t> uops(UOP_WORDS + 2);
     build_uops(prg.data(), dt, uops.data());
+    uops[UOP_WORDS] = uops[UOP_WORDS + 1] = 0xffffffffu;  // no such pc
+    for (uint32_t i = 0, k = 0; i < 0x8000u && k < 2; i++)
+        if (uops[2 * i] & UOP_IDLE) uops[UOP_WORDS + k++] = 0x8000u + i;
     cudaError_t e = cudaMemcpy(d_prg, prg.data(), 0x8000, cudaMemcpyHostToDevice);
-    if (e == cudaSuccess) e = cudaMemcpy(d_prg + PRG_UOP_OFF, uops.data(), (size_t)UOP_WORDS * 4, cudaMemcpyHostToDevice);
+    if (e == cudaSuccess) e = cudaMemcpy(d_prg + PRG_UOP_OFF, uops.data(), (size_t)(UOP_WORDS + 2) * 4, cudaMemcpyHostToDevice);
     return e;
 }
 

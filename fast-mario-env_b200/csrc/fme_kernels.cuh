@@ -90,6 +90,14 @@ __device__ __forceinline__ uint32_t sched_key(bool running, const Hot& h) {
     k = h.exec_at >= FRAME_ITERS ? 0x20000u : k;
     return running ? k : 0xffffffffu;
 }
+// The same key with the idle loops recognised by address (the ROM's first two `JMP *`, stored after its
+// micro-op table): it does not wait for the micro-op load of the new pc, so that load overlaps the vote.
+// Further idle loops only group less well; the key never changes what a lane computes.
+__device__ __forceinline__ uint32_t sched_key_pc(bool running, const Hot& h, uint32_t ip0, uint32_t ip1) {
+    uint32_t k = h.pc | ((h.pc == ip0) | (h.pc == ip1) ? 0x10000u : 0u);
+    k = h.exec_at >= FRAME_ITERS ? 0x20000u : k;
+    return running ? k : 0xffffffffu;
+}
 __device__ __forceinline__ bool minpc_turn(bool running, const Hot& h) {
     const uint32_t key = sched_key(running, h);
     const uint32_t mn = __reduce_min_sync(FULL, key);

@@ -58,6 +58,7 @@ PREVJOY = 0xFB
 JUMP = 0xFC
 XSCORE = 0xFD
 TMP2 = 0xFE
+IDLE_TMP = 0xFF       # idle_loops > 1 only
 STATUS = 0x0756
 LIVES = 0x075A
 STAGE = 0x075C
@@ -256,8 +257,15 @@ def _add_digits(a: Asm, base: int, ndig: int, pos: int, amount: int):
     a.label(done)
 
 
-def build_rom(seed: int = 0, divergence: bool = False, n_blocks: int = 256, pre_blocks: int = 96) -> bytes:
-    """Return the iNES image (16 + 32768 + 8192 bytes)."""
+def build_rom(seed: int = 0, divergence: bool = False, n_blocks: int = 256, pre_blocks: int = 96,
+              idle_loops: int = 1) -> bytes:
+    """Return the iNES image (16 + 32768 + 8192 bytes).
+
+    idle_loops=4 (test image): the main thread idles in one of four ``JMP *`` loops; at the end of every NMI
+    the handler rewrites the interrupted return address to loop (LFSR ^ controller) & 3, so envs wait in
+    different idle loops from frame to frame. The default image (1 loop) is unchanged by this option."""
+    if idle_loops not in (1, 4):
+        raise ValueError("idle_loops must be 1 or 4")
     rng = np.random.default_rng(seed)
     chr_ = bytearray(rng.integers(0, 256, 0x2000, dtype=np.uint8).tobytes())
     for bank in (0x0000, 0x1000):
@@ -342,6 +350,12 @@ def build_rom(seed: int = 0, divergence: bool = False, n_blocks: int = 256, pre_
     a.op("sta", "abs", 0x2001)
     a.label("main")
     a.op("jmp", "abs", "main")   # idle: the reference fast-forwards JMP-to-self exactly
+    if idle_loops > 1:           # three more idle loops right after it (3 bytes each, one page)
+        for k in range(1, idle_loops):
+            a.label(f"main{k}")
+            a.op("jmp", "abs", f"main{k}")
+        if (a.labels["main"] & 0xFF) > 0x100 - 3 * idle_loops:
+            raise ValueError("idle loops cross a page")
 
     # ------------------------------------------------------------------ shared subroutine for blocks
     a.label("sub")
@@ -479,6 +493,28 @@ def build_rom(seed: int = 0, divergence: bool = False, n_blocks: int = 256, pre_
     a.op("lda", "zp", TMP2)
     a.op("ora", "imm", 0x80)
     a.op("sta", "abs", 0x2000)
+    if idle_loops > 1:
+        # stack: $101+S = Y, X, A, P, PCL, PCH; an interrupted idle loop returns to loop (LFSR ^ JOY) & 3
+        a.op("tsx")
+        a.op("lda", "absx", 0x0106)
+        a.op("cmp", "imm", ">main")
+        a.op("bne", "rel", "nmi_keep")
+        a.op("lda", "absx", 0x0105)
+        a.op("sec")
+        a.op("sbc", "imm", "<main")
+        a.op("cmp", "imm", 3 * idle_loops)
+        a.op("bcs", "rel", "nmi_keep")
+        a.op("lda", "zp", LFSR_LO)
+        a.op("eor", "zp", JOY)
+        a.op("and", "imm", idle_loops - 1)
+        a.op("sta", "zp", IDLE_TMP)
+        a.op("asl", "acc")
+        a.op("clc")
+        a.op("adc", "zp", IDLE_TMP)
+        a.op("clc")
+        a.op("adc", "imm", "<main")
+        a.op("sta", "absx", 0x0105)
+        a.label("nmi_keep")
     a.op("pla")
     a.op("tay")
     a.op("pla")

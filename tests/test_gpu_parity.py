@@ -101,6 +101,10 @@ CONFIGS = {
     # 5 groups of 32 (the last ragged) in 4 step slices of uneven size
     "sliced_150": dict(levels=["1-1", "3-2", "5-4", "8-1", "2-2"] * 30, n=150,
                        kw=dict(sticky=0.25, noop_max=30, maxpool=True, max_steps=90)),
+    # four `JMP *` loops, envs parked in different ones from frame to frame: the scheduler's vote knows only
+    # the first two by address; which lanes it groups must not change any result
+    "four_idle_loops": dict(levels=["1-1", "4-2", "6-3", "8-4"] * 16, n=64,
+                            kw=dict(sticky=0.25, noop_max=30, maxpool=True), rom_kw=dict(idle_loops=4)),
 }
 
 
@@ -109,6 +113,9 @@ def test_env_lockstep_vs_oracle(oracle, rom, rom_div, name):
     import torch
     c = CONFIGS[name]
     romb = rom_div if c.get("div") else rom
+    if "rom_kw" in c:
+        from fast_mario_env_b200.synth_rom import build_rom
+        romb = build_rom(0, **c["rom_kw"])
     n, kw = c["n"], c["kw"]
     lv3 = [fme.decode_level(x) for x in c["levels"]]
     ref_env = oracle.RefVecEnv(romb, lv3, n, seed=7, **kw)

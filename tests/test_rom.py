@@ -44,6 +44,21 @@ def test_rom_runs_without_bad_ops(oracle, rom_div):
     assert r.bad_ops() == 0
 
 
+def test_four_idle_loop_image(oracle, rom):
+    """The test image with four `JMP *` loops: only the code after the main loop and the NMI tail differ, it
+    boots and runs on the reference engine without unimplemented opcodes."""
+    r4 = synth_rom.build_rom(0, idle_loops=4)
+    assert len(r4) == len(rom) and r4[:16] == rom[:16] and r4 != rom
+    assert oracle.boot_frames_bounded(r4, (1, 1, 1), cap=500) < 100
+    r = oracle.RefRaw(r4)
+    rng = np.random.default_rng(0)
+    for _ in range(300):
+        r.frame(int(rng.integers(0, 256)), False)
+    assert r.bad_ops() == 0
+    with pytest.raises(ValueError):
+        synth_rom.build_rom(0, idle_loops=3)
+
+
 def test_asm_encodings():
     a = Asm()
     a.label("top")

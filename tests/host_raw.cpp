@@ -1,0 +1,123 @@
+// Host build of the engine's emulation headers, used by the CPU test suite (tests/test_host_engine.py).
+//
+// Raw consoles are stepped one NES frame at a time with the code the GPU kernels run: Core (fme_core.h), the
+// register-resident fast path and its per-PC micro-ops (fme_fast.h, fme_tables.h) and the frame bookkeeping
+// of fme_agent.h. Each console has a whole group slab to itself and uses lane 0 of it, so memory is laid out
+// exactly as in the kernels. The per-frame flow follows k_raw: scalars in, begin_frame, hot_step until the
+// frame end, end_frame / close_frame, scalars out. No pixels are drawn (the GPU renderer is warp code); the
+// PPU log is produced and discarded, so its catch-up and logging paths still run.
+#include <cstdint>
+#include <cstring>
+#include <vector>
+
+#include "fme_core.h"
+#include "fme_agent.h"
+#include "fme_tables.h"
+#include "fme_fast.h"
+
+namespace fme { uint32_t g_host_dtab[256]; }
+using namespace fme;
+
+namespace {
+
+constexpr int kLogCap = 4096;
+
+struct HostRaw {
+    int n = 0;
+    std::vector<uint8_t> prg;      // 32 KB PRG, then the micro-op table (2 words per PRG address)
+    std::vector<uint8_t> chr;      // 8 KB
+    uint32_t nt[4] = {0, 0, 0, 0};
+    std::vector<uint8_t> slab;     // n x SLAB_BYTES, lane 0 of each used
+    std::vector<uint8_t> vram;     // n x VRAM_BYTES
+    std::vector<uint32_t> words;   // n x S_WORDS
+    std::vector<uint8_t> log;      // one log slot, reused by every console and frame
+};
+
+void bind(HostRaw* r, Core& c, int e) {
+    uint8_t* s = r->slab.data() + (size_t)e * SLAB_BYTES;
+    c.ram = s + SLAB_RAM_OFF;
+    c.oam = s + SLAB_OAM_OFF;
+    c.pal = s + SLAB_PAL_OFF;
+    c.vram = r->vram.data() + (size_t)e * VRAM_BYTES;
+    c.cart.prg = r->prg.data();
+    c.cart.chr = r->chr.data();
+    for (int i = 0; i < 4; i++) c.cart.nt[i] = r->nt[i];
+    c.rec = nullptr; c.nrec = 0; c.cap = 0; c.seg_open = false; c.seg_w0 = 0; c.seg_y1 = 0; c.status = 0;
+    c.seg_idx = 0; c.seg_reads = 0; c.vram_burst = 0; c.vram_dirty = false;
+}
+
+}  // namespace
+
+extern "C" {
+
+// iNES mapper 0 (16 or 32 KB PRG, 8 KB CHR, H/V mirroring) -> n consoles at power-on; NULL for other images.
+void* hr_create(const uint8_t* rom, int64_t len, int n) {
+    if (!rom || len < 16 || n < 1 || memcmp(rom, "NES\x1a", 4) != 0) return nullptr;
+    const int banks = rom[4], chr_banks = rom[5];
+    const int mapper = (rom[6] >> 4) | (rom[7] & 0xF0);
+    if (mapper != 0 || (banks != 1 && banks != 2) || chr_banks != 1) return nullptr;
+    const size_t off = 16 + ((rom[6] & 4) ? 512 : 0);
+    if ((size_t)len < off + (size_t)banks * 0x4000 + 0x2000) return nullptr;
+    HostRaw* r = new HostRaw;
+    r->n = n;
+    r->prg.assign(0x8000 + (size_t)UOP_WORDS * 4, 0);
+    for (int k = 0; k < 2; k++) memcpy(r->prg.data() + k * 0x4000, rom + off + (banks == 2 ? k : 0) * 0x4000, 0x4000);
+    r->chr.assign(rom + off + (size_t)banks * 0x4000, rom + off + (size_t)banks * 0x4000 + 0x2000);
+    if (rom[6] & 1) { r->nt[1] = r->nt[3] = 0x400; }   // vertical mirroring
+    else { r->nt[2] = r->nt[3] = 0x400; }               // horizontal mirroring
+    tables::build_dtab(g_host_dtab);
+    tables::build_uops(r->prg.data(), g_host_dtab, reinterpret_cast<uint32_t*>(r->prg.data() + 0x8000));
+    r->slab.assign((size_t)n * SLAB_BYTES, 0);
+    r->vram.assign((size_t)n * VRAM_BYTES, 0);
+    r->words.assign((size_t)n * S_WORDS, 0);
+    r->log.assign(slot_bytes(kLogCap), 0);
+    for (int e = 0; e < n; e++) {  // k_power
+        Core c;
+        bind(r, c, e);
+        c.bad_ops = 0;
+        c.power_on();
+        uint32_t* w = r->words.data() + (size_t)e * S_WORDS;
+        c.store_scalars(w);
+    }
+    return r;
+}
+
+// One frame of every console with the given controller bytes (k_raw without the renderer).
+void hr_frame(void* h, const uint8_t* buttons) {
+    HostRaw* r = static_cast<HostRaw*>(h);
+    for (int e = 0; e < r->n; e++) {
+        Core c;
+        bind(r, c, e);
+        uint32_t* w = r->words.data() + (size_t)e * S_WORDS;
+        c.load_scalars(w);
+        c.bad_ops = w[S_BADOPS];
+        c.status = w[S_STATUS];
+        uint8_t* slot = r->log.data();
+        begin_frame(c, slot, buttons[e], kLogCap);
+        const Fast fst{c.ram, r->prg.data(), reinterpret_cast<const uint32_t*>(r->prg.data() + 0x8000)};
+        Hot hot;
+        hot_in(hot, c, fst);
+        while (hot_step(hot, c, fst)) {
+        }
+        hot_out(hot, c);
+        c.end_frame();
+        close_frame(c, slot);
+        materialise_state(c);
+        c.store_scalars(w);
+        w[S_BADOPS] = c.bad_ops;
+        w[S_STATUS] = c.status;
+    }
+}
+
+void hr_ram(void* h, int e, uint8_t* out) {
+    HostRaw* r = static_cast<HostRaw*>(h);
+    Core c;
+    bind(r, c, e);
+    for (uint32_t a = 0; a < 0x800u; a++) out[a] = (uint8_t)c.RAM(a);
+}
+
+int64_t hr_bad_ops(void* h, int e) { return static_cast<HostRaw*>(h)->words[(size_t)e * S_WORDS + S_BADOPS]; }
+int64_t hr_status(void* h, int e) { return static_cast<HostRaw*>(h)->words[(size_t)e * S_WORDS + S_STATUS]; }
+void hr_destroy(void* h) { delete static_cast<HostRaw*>(h); }
+
+}  // extern "C"

@@ -711,6 +711,12 @@ uint64_t sticky_threshold(double sticky) {
 }  // namespace
 
 constexpr int kChunks = 4;
+struct HostFix {  // arguments of the host fix-up after fme_step_to_host's copies
+    uint8_t* obs = nullptr;
+    const uint8_t* term = nullptr;
+    const uint8_t* trunc = nullptr;
+    int n = 0, K = 0;
+};
 
 struct FmeEnv {
     FmeConfig cfg{};
@@ -734,6 +740,10 @@ struct FmeEnv {
     int nch = 0;
     cudaStream_t s_emu[kChunks] = {}, s_rnd[kChunks] = {};
     cudaEvent_t ev_in = nullptr, ev_emu[kChunks] = {}, ev_rnd[kChunks] = {};
+    // fme_step_to_host: early copy of the old frames (s_copy, one event per slice) and the host-side fix-up
+    cudaStream_t s_copy = nullptr;
+    cudaEvent_t ev_pre[kChunks] = {}, ev_copy = nullptr;
+    HostFix fix{};
     FmeBuffers buf{};
     bool bound = false;
     uint64_t sticky_thr = 0;
@@ -766,6 +776,10 @@ static void free_env(FmeEnv* v) {
         if (v->ev_rnd[c]) cudaEventDestroy(v->ev_rnd[c]);
     }
     if (v->ev_in) cudaEventDestroy(v->ev_in);
+    if (v->s_copy) cudaStreamDestroy(v->s_copy);
+    if (v->ev_copy) cudaEventDestroy(v->ev_copy);
+    for (int c = 0; c < kChunks; c++)
+        if (v->ev_pre[c]) cudaEventDestroy(v->ev_pre[c]);
     delete v;
 }
 
@@ -834,6 +848,9 @@ static int create_impl(const FmeConfig* cfg, const uint8_t* rom, int64_t rom_len
         const int groups = (C.n_envs + 31) / 32;
         v->nch = groups < kChunks ? groups : kChunks;
         CK(cudaEventCreateWithFlags(&v->ev_in, cudaEventDisableTiming));
+        CK(cudaStreamCreateWithPriority(&v->s_copy, cudaStreamNonBlocking, lo));
+        CK(cudaEventCreateWithFlags(&v->ev_copy, cudaEventDisableTiming));
+        for (int c = 0; c < v->nch; c++) CK(cudaEventCreateWithFlags(&v->ev_pre[c], cudaEventDisableTiming));
         for (int c = 0; c < v->nch; c++) {
             CK(cudaStreamCreateWithPriority(&v->s_emu[c], cudaStreamNonBlocking, hi));
             CK(cudaStreamCreateWithPriority(&v->s_rnd[c], cudaStreamNonBlocking, lo));
@@ -968,6 +985,16 @@ int fme_set_buffers(FmeEnv* v, const FmeBuffers* b) {
     return FME_OK;
 }
 
+// fme_step_to_host, after the last copy: an env whose episode ended restarts its stack as K-1 zero frames and
+// the reset frame; the early copy gave it the old frames, so they are cleared here (runs on a driver thread
+// once the copies are done, before the caller's stream moves on).
+static void CUDART_CB zero_restarted_stacks(void* arg) {
+    const HostFix* f = static_cast<const HostFix*>(arg);
+    const size_t ob = (size_t)f->K * OBS_BYTES;
+    for (int e = 0; e < f->n; e++)
+        if (f->term[e] | f->trunc[e]) memset(f->obs + (size_t)e * ob, 0, (size_t)(f->K - 1) * OBS_BYTES);
+}
+
 static int launch_step_like(FmeEnv* v, const int64_t* d_actions, void* stream, bool reset, void* mark = nullptr,
                             const FmeHostOut* host = nullptr) {
     if (!v) return fail(FME_E_ARG, "null env");
@@ -989,6 +1016,20 @@ static int launch_step_like(FmeEnv* v, const int64_t* d_actions, void* stream, b
         RenderParams R;
         R.d = d; R.jobs = v->d_jobs; R.obs = P.obs; R.fin = P.fin; R.cache_obs = P.cache.obs; R.frame_stack = P.frame_stack;
         CK(cudaEventRecord(v->ev_in, s));
+        const int K = v->K;
+        const size_t ob = (size_t)K * OBS_BYTES;
+        if (host && K > 1) {
+            // Frames 1..K-1 of every stack, still untouched on the device, are frames 0..K-2 of the new one: they
+            // go to the host while the envs emulate, leaving only each env's new frame for after its render.
+            CK(cudaStreamWaitEvent(v->s_copy, v->ev_in, 0));
+            for (int c = 0; c < v->nch; c++) {
+                const int g0 = groups * c / v->nch, g1 = groups * (c + 1) / v->nch;
+                const int e0 = g0 * 32, e1 = g1 * 32 < v->n ? g1 * 32 : v->n;
+                CK(cudaMemcpy2DAsync(host->obs + e0 * ob, ob, P.obs + e0 * ob + OBS_BYTES, ob, (size_t)(K - 1) * OBS_BYTES,
+                                     (size_t)(e1 - e0), cudaMemcpyDeviceToHost, v->s_copy));
+                CK(cudaEventRecord(v->ev_pre[c], v->s_copy));
+            }
+        }
         for (int c = 0; c < v->nch; c++) {
             const int g0 = groups * c / v->nch, g1 = groups * (c + 1) / v->nch;
             const int e0 = g0 * 32, e1 = g1 * 32 < v->n ? g1 * 32 : v->n;
@@ -997,12 +1038,14 @@ static int launch_step_like(FmeEnv* v, const int64_t* d_actions, void* stream, b
             k_step<true><<<g1 - g0, 32, STEP_SMEM, v->s_emu[c]>>>(P);
             CK(cudaEventRecord(v->ev_emu[c], v->s_emu[c]));
             CK(cudaStreamWaitEvent(v->s_rnd[c], v->ev_emu[c], 0));
+            if (host && K > 1) CK(cudaStreamWaitEvent(v->s_rnd[c], v->ev_pre[c], 0));  // old frames copied first
             R.env_base = e0;
             k_render<<<(unsigned)(e1 - e0) * NBANDS, 32, RB_BYTES, v->s_rnd[c]>>>(R);
             if (host) {  // this slice's outputs to the host while later slices still run
-                const size_t ob = (size_t)v->K * OBS_BYTES, ne = (size_t)(e1 - e0);
+                const size_t ne = (size_t)(e1 - e0), fo = (size_t)(K - 1) * OBS_BYTES;
                 cudaStream_t cs = v->s_rnd[c];
-                CK(cudaMemcpyAsync(host->obs + e0 * ob, P.obs + e0 * ob, ne * ob, cudaMemcpyDeviceToHost, cs));
+                CK(cudaMemcpy2DAsync(host->obs + e0 * ob + fo, ob, P.obs + e0 * ob + fo, ob, OBS_BYTES, ne,
+                                     cudaMemcpyDeviceToHost, cs));
                 CK(cudaMemcpyAsync(host->rew + e0, P.rew + e0, ne * 4, cudaMemcpyDeviceToHost, cs));
                 CK(cudaMemcpyAsync(host->term + e0, P.term + e0, ne, cudaMemcpyDeviceToHost, cs));
                 CK(cudaMemcpyAsync(host->trunc + e0, P.trunc + e0, ne, cudaMemcpyDeviceToHost, cs));
@@ -1015,6 +1058,13 @@ static int launch_step_like(FmeEnv* v, const int64_t* d_actions, void* stream, b
         if (mark) {  // all emulation slices done (renders may already be running)
             for (int c = 1; c < v->nch; c++) CK(cudaStreamWaitEvent(v->s_emu[0], v->ev_emu[c], 0));
             CK(cudaEventRecord((cudaEvent_t)mark, v->s_emu[0]));
+        }
+        if (host && K > 1) {
+            for (int c = 0; c < v->nch; c++) CK(cudaStreamWaitEvent(v->s_copy, v->ev_rnd[c], 0));
+            v->fix.obs = host->obs; v->fix.term = host->term; v->fix.trunc = host->trunc; v->fix.n = v->n; v->fix.K = K;
+            CK(cudaLaunchHostFunc(v->s_copy, zero_restarted_stacks, &v->fix));
+            CK(cudaEventRecord(v->ev_copy, v->s_copy));
+            CK(cudaStreamWaitEvent(s, v->ev_copy, 0));
         }
         for (int c = 0; c < v->nch; c++) CK(cudaStreamWaitEvent(s, v->ev_rnd[c], 0));
     }

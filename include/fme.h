@@ -112,10 +112,12 @@ typedef struct FmeHostOut {
     double* ep_ret;
     int32_t* ep_len;
 } FmeHostOut;
-/* fme_step, and each env slice's outputs copied into pinned host memory as soon as that slice's kernels are
- * done, so the copies overlap the later slices' work. Replaces fm_step_async + fm_step_wait's host-buffer
- * outputs (csrc/fastmario.cpp:611-617) for callers that want host arrays. Async: synchronise the stream before
- * reading `out`. */
+/* fme_step, and the step's outputs copied into pinned host memory while the step runs: frames 1..k-1 of every
+ * stack (frames 0..k-2 of the new one) as soon as the step starts, each slice's new frames and scalars once
+ * that slice's kernels are done, and, last, a host function (cudaLaunchHostFunc) clears frames 0..k-2 of the
+ * envs whose episode ended (their stack restarts as zeros + the reset frame). Replaces fm_step_async +
+ * fm_step_wait's host-buffer outputs (csrc/fastmario.cpp:611-617) for callers that want host arrays. Async:
+ * synchronise the stream before reading `out`. */
 int fme_step_to_host(FmeEnv* env, const int64_t* d_actions, const FmeHostOut* out, void* stream);
 
 /* OR of the device status bits of all envs since create (call after synchronising). */

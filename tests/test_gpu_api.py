@@ -96,6 +96,29 @@ def test_step_arrays_matches_step(rom):
     f.close(); g.close()
 
 
+def test_host_outputs_match_device_outputs_across_slices(rom):
+    """fme_step_to_host (early copy of the old frames, new frame after the render, stacks of restarted episodes
+    cleared on the host) against the device buffers of fme_step: 150 envs = 4 step slices, short episodes."""
+    import torch
+    levels = ["1-1", "3-2", "5-4", "8-1", "2-2"] * 30
+    kw = dict(seed=11, sticky=0.25, noop_max=30, maxpool=True, max_steps=25, rom=rom)
+    f = fme.FastVecEnv(levels, 150, **kw)
+    d = fme.CudaVecEnv(levels, 150, **kw)
+    assert np.array_equal(f.reset(), d.reset().cpu().numpy())
+    rng = np.random.default_rng(12)
+    ended = 0
+    for _ in range(60):
+        a = rng.integers(0, 7, 150)
+        o1, r1, te1, tr1, inf1, _ = f.step_arrays(a)
+        o2, r2, te2, tr2, _ = d.step(torch.from_numpy(a).cuda())
+        assert np.array_equal(o1, o2.cpu().numpy()) and np.array_equal(r1, r2.cpu().numpy())
+        assert np.array_equal(te1, te2.cpu().numpy()) and np.array_equal(tr1, tr2.cpu().numpy())
+        assert np.array_equal(inf1, d.info_t.cpu().numpy())
+        ended += int((te1 | tr1).sum())
+    assert ended > 50
+    f.close(); d.close()
+
+
 def test_resize_matches_cv2_golden():
     g = np.load(os.path.join(GOLD, "resize.npz"))
     out = fme.resize_area(g["src"])

@@ -711,6 +711,7 @@ uint64_t sticky_threshold(double sticky) {
 }  // namespace
 
 constexpr int kChunks = 4;
+constexpr int kTailParts = 4;   // fme_step_to_host renders the last slice in this many parts
 struct HostFix {  // arguments of the host fix-up after fme_step_to_host's copies
     uint8_t* obs = nullptr;
     const uint8_t* term = nullptr;
@@ -742,7 +743,7 @@ struct FmeEnv {
     cudaEvent_t ev_in = nullptr, ev_emu[kChunks] = {}, ev_rnd[kChunks] = {};
     // fme_step_to_host: early copy of the old frames (s_copy, one event per slice) and the host-side fix-up
     cudaStream_t s_copy = nullptr;
-    cudaEvent_t ev_pre[kChunks] = {}, ev_copy = nullptr;
+    cudaEvent_t ev_pre[kChunks] = {}, ev_copy = nullptr, ev_part[kTailParts] = {};
     HostFix fix{};
     FmeBuffers buf{};
     bool bound = false;
@@ -780,6 +781,8 @@ static void free_env(FmeEnv* v) {
     if (v->ev_copy) cudaEventDestroy(v->ev_copy);
     for (int c = 0; c < kChunks; c++)
         if (v->ev_pre[c]) cudaEventDestroy(v->ev_pre[c]);
+    for (int q = 0; q < kTailParts; q++)
+        if (v->ev_part[q]) cudaEventDestroy(v->ev_part[q]);
     delete v;
 }
 
@@ -851,6 +854,7 @@ static int create_impl(const FmeConfig* cfg, const uint8_t* rom, int64_t rom_len
         CK(cudaStreamCreateWithPriority(&v->s_copy, cudaStreamNonBlocking, lo));
         CK(cudaEventCreateWithFlags(&v->ev_copy, cudaEventDisableTiming));
         for (int c = 0; c < v->nch; c++) CK(cudaEventCreateWithFlags(&v->ev_pre[c], cudaEventDisableTiming));
+        for (int q = 0; q < kTailParts; q++) CK(cudaEventCreateWithFlags(&v->ev_part[q], cudaEventDisableTiming));
         for (int c = 0; c < v->nch; c++) {
             CK(cudaStreamCreateWithPriority(&v->s_emu[c], cudaStreamNonBlocking, hi));
             CK(cudaStreamCreateWithPriority(&v->s_rnd[c], cudaStreamNonBlocking, lo));
@@ -985,6 +989,17 @@ int fme_set_buffers(FmeEnv* v, const FmeBuffers* b) {
     return FME_OK;
 }
 
+// Per-env scalar outputs of envs [e0, e0 + ne) to the caller's pinned host buffers, on stream cs.
+static cudaError_t copy_scalars(const StepParams& P, const FmeHostOut* host, int e0, size_t ne, cudaStream_t cs) {
+    cudaError_t e = cudaMemcpyAsync(host->rew + e0, P.rew + e0, ne * 4, cudaMemcpyDeviceToHost, cs);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(host->term + e0, P.term + e0, ne, cudaMemcpyDeviceToHost, cs);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(host->trunc + e0, P.trunc + e0, ne, cudaMemcpyDeviceToHost, cs);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(host->info + e0 * 10, P.info + e0 * 10, ne * 40, cudaMemcpyDeviceToHost, cs);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(host->ep_ret + e0, P.ep_ret + e0, ne * 8, cudaMemcpyDeviceToHost, cs);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(host->ep_len + e0, P.ep_len + e0, ne * 4, cudaMemcpyDeviceToHost, cs);
+    return e;
+}
+
 // fme_step_to_host, after the last copy: an env whose episode ended restarts its stack as K-1 zero frames and
 // the reset frame; the early copy gave it the old frames, so they are cleared here (runs on a driver thread
 // once the copies are done, before the caller's stream moves on).
@@ -1039,6 +1054,25 @@ static int launch_step_like(FmeEnv* v, const int64_t* d_actions, void* stream, b
             CK(cudaEventRecord(v->ev_emu[c], v->s_emu[c]));
             CK(cudaStreamWaitEvent(v->s_rnd[c], v->ev_emu[c], 0));
             if (host && K > 1) CK(cudaStreamWaitEvent(v->s_rnd[c], v->ev_pre[c], 0));  // old frames copied first
+            if (host && K > 1 && v->nch > 1 && c == v->nch - 1) {
+                // the last slice's copies are the ones nothing hides: its scalars go as soon as it has emulated,
+                // and it is rendered in parts, each part's new frames copied while the next part renders
+                const size_t fo = (size_t)(K - 1) * OBS_BYTES;
+                CK(cudaStreamWaitEvent(v->s_copy, v->ev_emu[c], 0));
+                CK(copy_scalars(P, host, e0, (size_t)(e1 - e0), v->s_copy));
+                for (int q = 0; q < kTailParts; q++) {
+                    const int q0 = e0 + (e1 - e0) * q / kTailParts, q1 = e0 + (e1 - e0) * (q + 1) / kTailParts;
+                    if (q1 <= q0) continue;
+                    R.env_base = q0;
+                    k_render<<<(unsigned)(q1 - q0) * NBANDS, 32, RB_BYTES, v->s_rnd[c]>>>(R);
+                    CK(cudaEventRecord(v->ev_part[q], v->s_rnd[c]));
+                    CK(cudaStreamWaitEvent(v->s_copy, v->ev_part[q], 0));
+                    CK(cudaMemcpy2DAsync(host->obs + q0 * ob + fo, ob, P.obs + q0 * ob + fo, ob, OBS_BYTES,
+                                         (size_t)(q1 - q0), cudaMemcpyDeviceToHost, v->s_copy));
+                }
+                CK(cudaEventRecord(v->ev_rnd[c], v->s_rnd[c]));
+                continue;
+            }
             R.env_base = e0;
             k_render<<<(unsigned)(e1 - e0) * NBANDS, 32, RB_BYTES, v->s_rnd[c]>>>(R);
             if (host) {  // this slice's outputs to the host while later slices still run
@@ -1046,12 +1080,7 @@ static int launch_step_like(FmeEnv* v, const int64_t* d_actions, void* stream, b
                 cudaStream_t cs = v->s_rnd[c];
                 CK(cudaMemcpy2DAsync(host->obs + e0 * ob + fo, ob, P.obs + e0 * ob + fo, ob, OBS_BYTES, ne,
                                      cudaMemcpyDeviceToHost, cs));
-                CK(cudaMemcpyAsync(host->rew + e0, P.rew + e0, ne * 4, cudaMemcpyDeviceToHost, cs));
-                CK(cudaMemcpyAsync(host->term + e0, P.term + e0, ne, cudaMemcpyDeviceToHost, cs));
-                CK(cudaMemcpyAsync(host->trunc + e0, P.trunc + e0, ne, cudaMemcpyDeviceToHost, cs));
-                CK(cudaMemcpyAsync(host->info + e0 * 10, P.info + e0 * 10, ne * 40, cudaMemcpyDeviceToHost, cs));
-                CK(cudaMemcpyAsync(host->ep_ret + e0, P.ep_ret + e0, ne * 8, cudaMemcpyDeviceToHost, cs));
-                CK(cudaMemcpyAsync(host->ep_len + e0, P.ep_len + e0, ne * 4, cudaMemcpyDeviceToHost, cs));
+                CK(copy_scalars(P, host, e0, ne, cs));
             }
             CK(cudaEventRecord(v->ev_rnd[c], v->s_rnd[c]));
         }

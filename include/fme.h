@@ -114,7 +114,7 @@ typedef struct FmeHostOut {
 } FmeHostOut;
 /* fme_step, and the step's outputs copied into pinned host memory while the step runs: frames 1..k-1 of every
  * stack (frames 0..k-2 of the new one) as soon as the step starts, each slice's new frames and scalars once
- * that slice's kernels are done, and, last, a host function (cudaLaunchHostFunc) clears frames 0..k-2 of the
+ * that slice's kernels are done (the last slice rendered and copied in parts), and, last, a host function (cudaLaunchHostFunc) clears frames 0..k-2 of the
  * envs whose episode ended (their stack restarts as zeros + the reset frame). Replaces fm_step_async +
  * fm_step_wait's host-buffer outputs (csrc/fastmario.cpp:611-617) for callers that want host arrays. Async:
  * synchronise the stream before reading `out`. */

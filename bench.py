@@ -434,7 +434,10 @@ def main():
         line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
                 "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak",
                 "vs_baseline": None, "dtype": "u8", "data": "synthetic", "config": workload(args),
-                "parallelism": f"env shards by env_offset x{world}, no collective", "gpu_launches": 2 * args.steps,
+                "parallelism": f"env shards by env_offset x{world}, no collective",
+                # per step and GPU: an emulation and a render launch for each of the library's step slices
+                # (4, or one per 32-env group below 128 envs)
+                "gpu_launches": 2 * min((E + 31) // 32, 4) * args.steps,
                 "roofline": roofline, "cpu_baseline": cb, "e2e": e2e, "clocks": clk}
         if ref_cuda is not None:
             line["reference_cuda"] = ref_cuda

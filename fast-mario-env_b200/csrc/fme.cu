@@ -744,7 +744,10 @@ struct FmeEnv {
     // fme_step_to_host: early copy of the old frames (s_copy, one event per slice) and the host-side fix-up
     cudaStream_t s_copy = nullptr;
     cudaEvent_t ev_pre[kChunks] = {}, ev_copy = nullptr, ev_part[kTailParts] = {};
-    HostFix fix{};
+    // one argument block per call still in flight (calls enqueued back to back may name other host buffers)
+    static constexpr int kFixRing = 16;
+    HostFix fix[kFixRing] = {};
+    uint32_t fix_next = 0;
     FmeBuffers buf{};
     bool bound = false;
     uint64_t sticky_thr = 0;
@@ -1090,8 +1093,9 @@ static int launch_step_like(FmeEnv* v, const int64_t* d_actions, void* stream, b
         }
         if (host && K > 1) {
             for (int c = 0; c < v->nch; c++) CK(cudaStreamWaitEvent(v->s_copy, v->ev_rnd[c], 0));
-            v->fix.obs = host->obs; v->fix.term = host->term; v->fix.trunc = host->trunc; v->fix.n = v->n; v->fix.K = K;
-            CK(cudaLaunchHostFunc(v->s_copy, zero_restarted_stacks, &v->fix));
+            HostFix* fx = &v->fix[v->fix_next++ % FmeEnv::kFixRing];
+            fx->obs = host->obs; fx->term = host->term; fx->trunc = host->trunc; fx->n = v->n; fx->K = K;
+            CK(cudaLaunchHostFunc(v->s_copy, zero_restarted_stacks, fx));
             CK(cudaEventRecord(v->ev_copy, v->s_copy));
             CK(cudaStreamWaitEvent(s, v->ev_copy, 0));
         }

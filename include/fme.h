@@ -117,7 +117,7 @@ typedef struct FmeHostOut {
  * that slice's kernels are done (the last slice rendered and copied in parts), and, last, a host function (cudaLaunchHostFunc) clears frames 0..k-2 of the
  * envs whose episode ended (their stack restarts as zeros + the reset frame). Replaces fm_step_async +
  * fm_step_wait's host-buffer outputs (csrc/fastmario.cpp:611-617) for callers that want host arrays. Async:
- * synchronise the stream before reading `out`. */
+ * synchronise the stream before reading `out`; at most 16 calls of one env may be in flight at once. */
 int fme_step_to_host(FmeEnv* env, const int64_t* d_actions, const FmeHostOut* out, void* stream);
 
 /* OR of the device status bits of all envs since create (call after synchronising). */

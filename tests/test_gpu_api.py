@@ -119,6 +119,47 @@ def test_host_outputs_match_device_outputs_across_slices(rom):
     f.close(); d.close()
 
 
+def test_step_to_host_back_to_back_with_two_buffer_sets(rom):
+    """Two fme_step_to_host calls enqueued without a sync in between, into different pinned buffer sets: each
+    set must hold its own step's outputs (the host fix-up of the first call must not use the second's)."""
+    import ctypes
+    import torch
+    from fast_mario_env_b200 import _native as N
+    levels = ["1-1", "3-2", "5-4", "8-1", "2-2"] * 30
+    kw = dict(seed=21, sticky=0.25, noop_max=30, maxpool=True, max_steps=15, rom=rom)
+    h = fme.CudaVecEnv(levels, 150, **kw)
+    d = fme.CudaVecEnv(levels, 150, **kw)
+    h.reset(); d.reset()
+    pin = dict(pin_memory=True)
+
+    def bufs():
+        t = (torch.zeros(150, 4, 84, 84, dtype=torch.uint8, **pin), torch.zeros(150, dtype=torch.float32, **pin),
+             torch.zeros(150, dtype=torch.bool, **pin), torch.zeros(150, dtype=torch.bool, **pin),
+             torch.zeros(150, len(fme.INFO_FIELDS), dtype=torch.int32, **pin),
+             torch.zeros(150, dtype=torch.float64, **pin), torch.zeros(150, dtype=torch.int32, **pin))
+        return t, N.FmeHostOut(*[x.data_ptr() for x in t])
+
+    (ta, oa), (tb, ob) = bufs(), bufs()
+    rng = np.random.default_rng(22)
+    ended = 0
+    for _ in range(30):
+        a1 = torch.from_numpy(rng.integers(0, 7, 150)).cuda()
+        a2 = torch.from_numpy(rng.integers(0, 7, 150)).cuda()
+        h.actions.copy_(a1)
+        N.check(N.lib().fme_step_to_host(h.h, N.ptr(h.actions), ctypes.byref(oa), h._stream()), "step_to_host")
+        h.actions.copy_(a2)
+        N.check(N.lib().fme_step_to_host(h.h, N.ptr(h.actions), ctypes.byref(ob), h._stream()), "step_to_host")
+        torch.cuda.synchronize()
+        for act, (t, _) in ((a1, (ta, oa)), (a2, (tb, ob))):
+            o, r, te, tr, _ = d.step(act)
+            assert torch.equal(t[0], o.cpu()) and torch.equal(t[1], r.cpu())
+            assert torch.equal(t[2].to(torch.uint8), te.cpu().to(torch.uint8))
+            assert torch.equal(t[3].to(torch.uint8), tr.cpu().to(torch.uint8))
+            ended += int((t[2] | t[3]).sum())
+    assert ended > 50
+    h.close(); d.close()
+
+
 def test_resize_matches_cv2_golden():
     g = np.load(os.path.join(GOLD, "resize.npz"))
     out = fme.resize_area(g["src"])

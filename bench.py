@@ -33,9 +33,10 @@ METRIC = "agent env-steps/sec (skip 4, 84x84x4 obs)"
 UNIT = "env-steps/s"
 # algorithmic HBM bytes per env-step of each kernel of the step:
 #   k_step   console state in and out (RAM+OAM+palette 2336 B and VRAM 2048 B each way, 37 scalar words each
-#            way), the frame-stack shift (3 x 7056 B read and written), actions and outputs (58 B)
-#   k_render the new 84x84 frame (7056 B) and the job word (the PPU logs it replays are the emulation
-#            kernel's intermediate output, not counted)
+#            way), actions and outputs (58 B) and the render job word (4 B)
+#   k_render the frame-stack shift (frames 1..3 read and written to 0..2, 3 x 7056 B each way), the new 84x84
+#            frame (7056 B) and the job word (the PPU logs it replays are the emulation kernel's intermediate
+#            output, not counted)
 ALGO_BYTES = {"k_step": 2 * (2336 + 2048) + 2 * 37 * 4 + 58 + 4, "k_render": 2 * 3 * 7056 + 7056 + 4}
 
 
@@ -72,15 +73,42 @@ def read_peaks():
     return 6650.0, "fallback"
 
 
-def committed_traffic(kernel):
-    """DRAM bytes per env-step of `kernel` from its committed ncu summary (read + write of a small-case
-    capture scaled by env count: per-env state, stack and log traffic grow in proportion to the envs)."""
+def profile_figure(kernel, key):
+    """A per-env-step figure of `kernel` from its committed ncu summary (profiles/<kernel>_full_config1_4096.md,
+    lines `key = value`): DRAM bytes (read + write) and thread-instructions of a small-case capture, per env-step,
+    which grow in proportion to the envs."""
     p = os.path.join(ROOT, "profiles", f"{kernel}_full_config1_4096.md")
     if os.path.exists(p):
         for line in open(p):
-            if line.startswith("traffic_per_env_step_bytes"):
+            if line.startswith(key + " "):
                 return float(line.split("=")[1])
     return None
+
+
+def committed_traffic(kernel):
+    return profile_figure(kernel, "traffic_per_env_step_bytes")
+
+
+def issue_roofline(per_gpu_value, clk, sm_count):
+    """The roof that binds this branchy integer interpreter: useful-lane issue slots. achieved = the step's
+    thread-instructions per env-step (both kernels, from the committed ncu captures) x env-steps/s of one GPU;
+    peak = SMs x 4 schedulers x 32 lanes x the median SM clock sampled during the timed region."""
+    f_mhz = (clk or {}).get("sm_mhz") or 0.0
+    if not f_mhz:
+        return None
+    per = {k: profile_figure(k, "thread_inst_per_env_step") for k in ("k_step", "k_render")}
+    lanes = {k: profile_figure(k, "lanes_per_inst") for k in ("k_step", "k_render")}
+    if any(v is None for v in per.values()):
+        return None
+    peak = sm_count * 4 * 32 * f_mhz * 1e6
+    achieved = sum(per.values()) * per_gpu_value
+    return {"bound": "issue", "unit": "thread-inst/s", "achieved": achieved, "peak": peak, "frac": achieved / peak,
+            "per_kernel_frac": {k: v * per_gpu_value / peak for k, v in per.items()},
+            "thread_inst_per_env_step": per,
+            "warp_exec_efficiency": {k: (v / 32.0 if v else None) for k, v in lanes.items()},
+            "sm_count": sm_count, "sm_mhz": f_mhz,
+            "source": "thread-instructions per env-step and lanes per instruction from the committed ncu captures "
+                      "(profiles/*_full_config1_4096.md); env-steps/s and clock from this run"}
 
 
 class ClockSampler:
@@ -315,7 +343,10 @@ def main():
     ap.add_argument("--divergent", action="store_true",
                     help="config 2: the divergence-stress image (controller/LFSR-dependent control flow and sprites)")
     ap.add_argument("--ref-gpu", action="store_true",
-                    help="also time the reference's CudaVecEnv (baseline/_ref) against this engine at maxpool=False")
+                    help="time the reference's CudaVecEnv (baseline/_ref) against this engine at maxpool=False "
+                         "(on by default at one GPU; kept for compatibility)")
+    ap.add_argument("--no-ref-gpu", action="store_true",
+                    help="skip the reference CudaVecEnv arm that the default 1-GPU run times beside this engine")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
@@ -359,6 +390,8 @@ def main():
         env.step(acts[t])
     torch.cuda.synchronize(dev)
     env.check()
+    instr0, emu0 = env.work_counters()
+    frames0 = env.frames
     if dist:
         dist.barrier()
     # per step: an event before it and one between its two kernels (fme_step_marked), for the per-kernel times
@@ -380,6 +413,15 @@ def main():
     emu_ms = sum(starts[i].elapsed_time(mids[i]) for i in range(args.steps)) / args.steps
     rend_ms = sum(mids[i].elapsed_time(starts[i + 1] if i + 1 < args.steps else ev1) for i in range(args.steps)) / args.steps
     env.check()
+    instr1, emu1 = env.work_counters()
+    frames1 = env.frames
+    env_steps = E * args.steps
+    work = {"instructions_per_env_step": (instr1 - instr0) / env_steps,
+            "emulated_frames_per_env_step": (emu1 - emu0) / env_steps,
+            "reference_frames_per_env_step": (frames1 - frames0) / env_steps,
+            "note": "device counters over the timed steps: 6502 instructions executed (idle-loop fast-forward and "
+                    "sprite-0 poll skip excluded) and NES frames run by the step kernel; reference_frames also "
+                    "counts the no-op-start frames served from the reset cache and re-emulated frames, as fm_frames"}
     if dist:
         dist.barrier()
     ms_max = shard.max_over_ranks(ms, device=dev)
@@ -422,13 +464,17 @@ def main():
                 "traffic": traffic_per_step * E if traffic_per_step else None,
                 "kernel": top, "kernel_ms": kernel_ms, "algorithmic_bytes_per_env_step": ALGO_BYTES[top],
                 "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured" else "fallback 6.65 TB/s",
-                "note": "the env step is an issue-bound integer interpreter; HBM fraction is reported as required, "
-                        "issue-slot figures are in profiles/"}
+                "note": "the env step is an issue-bound integer interpreter: the HBM fraction is reported as the "
+                        "contract asks, the binding roof is roofline.issue"}
+    work["emulated_instructions_per_s"] = work["instructions_per_env_step"] * value
+    issue = issue_roofline(value / world, clk, torch.cuda.get_device_properties(dev).multi_processor_count)
+    if issue is not None:
+        roofline["issue"] = issue
     cb = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cb = cpu_baseline(rom, args)
     ref_cuda = None
-    if args.ref_gpu and rank == 0 and world == 1:
+    if rank == 0 and world == 1 and not args.no_ref_gpu and not args.divergent:
         ref_cuda = reference_cuda(rom, E, args.steps, args.warmup, dev)
     if rank == 0:
         line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
@@ -438,7 +484,7 @@ def main():
                 # per step and GPU: an emulation and a render launch for each of the library's step slices
                 # (4, or one per 32-env group below 128 envs)
                 "gpu_launches": 2 * min((E + 31) // 32, 4) * args.steps,
-                "roofline": roofline, "cpu_baseline": cb, "e2e": e2e, "clocks": clk}
+                "roofline": roofline, "cpu_baseline": cb, "e2e": e2e, "clocks": clk, "work": work}
         if ref_cuda is not None:
             line["reference_cuda"] = ref_cuda
         print(json.dumps(line))

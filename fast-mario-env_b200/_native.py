@@ -22,6 +22,9 @@ ST_LOG_OVERFLOW = 1
 ST_HACK_CAP = 2
 ST_BOOT_CAP = 4
 ST_BAD_ACTION = 8
+# capacity of the allocation-free raw frame call (include/fme.h FME_STATIC_*)
+FME_STATIC_MAX_CONSOLES = 64
+FME_STATIC_LOG_CAPACITY = 2048
 STATUS_NAMES = {ST_LOG_OVERFLOW: "PPU log overflow (raise log_capacity)",
                 ST_HACK_CAP: "busy-state skip loop exceeded hack_cap frames",
                 ST_BOOT_CAP: "level boot exceeded boot_cap frames",
@@ -38,6 +41,7 @@ SIGNATURES = {
     "fme_ram_all": (_i32, [_P, _P, _P]),
     "fme_frames": (_i32, [_P, _P]),
     "fme_bad_ops": (_i32, [_P, _P]),
+    "fme_work_counters": (_i32, [_P, _P, _P]),
     "fme_env_bytes": (_i64, [_P]),
     "fme_destroy": (None, [_P]),
     "fme_raw_create": (_i32, [_P, _i64, _i32, _i32, _i32, _P]),
@@ -70,8 +74,11 @@ class FmeConfig(ctypes.Structure):
                 ("hack_cap", _i32), ("boot_cap", _i32)]
 
 
+FME_HOST_OBS_IN_PLACE = 1
+
+
 class FmeHostOut(ctypes.Structure):
-    _fields_ = [(f, _P) for f in ("obs", "rew", "term", "trunc", "info", "ep_ret", "ep_len")]
+    _fields_ = [(f, _P) for f in ("obs", "rew", "term", "trunc", "info", "ep_ret", "ep_len")] + [("flags", _u32)]
 
 
 class FmeReplayBufs(ctypes.Structure):

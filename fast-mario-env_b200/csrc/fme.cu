@@ -1,22 +1,31 @@
 // fme.cu - kernels and the C ABI (include/fme.h) of libfme_cuda.so.
 //
-// Kernels (all warp-per-32-envs, one CTA = one warp, 73 KB of shared memory per CTA, 3 CTAs per SM):
-//   k_step    the fused agent step: load the group's RAM/OAM/palette slab into shared memory, emulate
-//             `skip` frames (+ busy-state frames) per env with per-frame PPU logs, bookkeeping, auto-reset
-//             from the reset cache, write the slab back, then replay the logs warp-cooperatively into a
-//             shared-memory framebuffer (max-pooled), area-resize to 84x84 and update the frame stacks.
-//   k_boot    boot each distinct level from power-on (the SMB boot protocol), snapshot + first obs.
-//   k_init    put every env at its level snapshot (the reference's Env::init state).
-//   k_reset   random no-op starts from the reset cache + zero-padded stacks (fm_reset).
-//   k_raw     one frame for n raw consoles (+ palette-value screens).
-//   k_resize, k_ram_all   helpers.
+// The timed step (fme_step) is two kernels per env slice (up to four slices, each forked from the caller's
+// stream onto a high-priority emulation stream and a low-priority render stream, joined back with events):
+//   k_step<true>   emulation, one CTA = one warp = 32 envs: the group's 64 KB of RAM in shared memory (OAM and
+//                  palette read through L1 from the HBM slab), `skip` frames (+ busy-state frames) per env with
+//                  per-frame PPU logs, rewards / dones / infos, auto-reset from the reset cache, and a render job
+//                  word per env.
+//   k_render       one warp per (env, band of 60 screen rows): the frame-stack shift of the band, replay of the
+//                  PPU log(s) into the band's rows (max-pooled), the exact-order INTER_AREA resize and the store
+//                  of the band's 21 rows of the new 84x84 frame (into final_obs when the episode ended).
+// Construction and API helpers:
+//   k_boot         boot each distinct level from power-on (the SMB boot protocol), snapshot + first obs.
+//   k_step<false>  the reset-cache builder (no-op steps with the renderer fused, one CTA per 32 levels).
+//   k_init         put every env at its level snapshot (the reference's Env::init state).
+//   k_reset        random no-op starts from the reset cache + zero-padded stacks (fm_reset).
+//   k_raw          one frame for n raw consoles (+ palette-value screens).
+//   k_resize, k_ram_all, k_power   helpers.
 #include <cuda_runtime.h>
 #include <math.h>
 #include <stdio.h>
 #include <string.h>
 #include <algorithm>
+#include <condition_variable>
+#include <functional>
 #include <mutex>
 #include <string>
+#include <thread>
 #include <vector>
 
 #include "fme_kernels.cuh"
@@ -68,6 +77,7 @@ __global__ void __launch_bounds__(32) k_boot(BootParams P) {
     // then loop B {4: fa(8), 5: fa(0)} while time >= tl.
     const Fast fst{c.ram, d.prg, d.uop};
     Hot h;
+    h.icount = 0;
     hot_in(h, c, fst);
     while (__any_sync(FULL, running)) {
         if (minpc_turn(running, h)) {
@@ -179,6 +189,8 @@ __global__ void __launch_bounds__(32, 1) k_step(StepParams P) {
     const Fast fst{c.ram, d.prg, d.uop};
     const uint32_t ip0 = __ldg(d.uop + UOP_WORDS), ip1 = __ldg(d.uop + UOP_WORDS + 1);
     Hot h;
+    h.icount = 0;
+    uint32_t emu_frames = 0;
     hot_in(h, c, fst);
     for (;;) {
         const uint32_t key = sched_key_pc(running, h, ip0, ip1);
@@ -187,6 +199,7 @@ __global__ void __launch_bounds__(32, 1) k_step(StepParams P) {
         if (key == mn && !hot_step(h, c, fst)) {
             hot_out(h, c);
             c.end_frame();
+            emu_frames++;
             running = ag.on_frame_end(c, ev, cfg);
             hot_in(h, c, fst);
         }
@@ -241,6 +254,11 @@ __global__ void __launch_bounds__(32, 1) k_step(StepParams P) {
         c.store_scalars(w);
         ev.store(w);
         w[S_BADOPS] = c.bad_ops; w[S_STATUS] = c.status;
+        // work counters: read back here rather than kept live across the emulation loop
+        const uint64_t ic = ((uint64_t)d.scal[(size_t)S_INSTR_HI * d.n_pad + e] << 32 |
+                             d.scal[(size_t)S_INSTR_LO * d.n_pad + e]) + h.icount;
+        w[S_INSTR_LO] = (uint32_t)ic; w[S_INSTR_HI] = (uint32_t)(ic >> 32);
+        w[S_EMU_FRAMES] = d.scal[(size_t)S_EMU_FRAMES * d.n_pad + e] + emu_frames;
         store_words(d, e, w);
         if (c.status) atomicOr(d.err, c.status);
     }
@@ -488,6 +506,7 @@ __global__ void __launch_bounds__(32) k_raw(RawParams P) {
     if (active) begin_frame(c, slot, P.buttons[e], d.log_cap);
     const Fast fst{c.ram, d.prg, d.uop};
     Hot h;
+    h.icount = 0;
     hot_in(h, c, fst);
     while (__any_sync(FULL, running)) {
         if (minpc_turn(running, h) && !hot_step(h, c, fst)) {
@@ -580,20 +599,53 @@ int fail(int code, const std::string& msg) { g_err = msg; return code; }
         if (_e != cudaSuccess) return fail(FME_E_CUDA, std::string(#call) + ": " + cudaGetErrorString(_e)); \
     } while (0)
 
+// Per-device set-up (constant tables, the static scratch address) belongs to the device's CUDA context: a
+// cudaDeviceReset destroys the primary context and with it both. The caches are therefore keyed by the unique
+// id of the context current at the call (cuCtxGetId, through the runtime's driver entry points so that the
+// library does not link libcuda), not by the device ordinal alone.
+typedef int (*PfnCtxGetCurrent)(void**);
+typedef int (*PfnCtxGetId)(void*, unsigned long long*);
+int current_context_id(unsigned long long* id) {
+    static PfnCtxGetCurrent get_current = nullptr;
+    static PfnCtxGetId get_id = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        cudaDriverEntryPointQueryResult q;
+        void* f = nullptr;
+        if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &f, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            get_current = reinterpret_cast<PfnCtxGetCurrent>(f);
+        f = nullptr;
+        if (cudaGetDriverEntryPoint("cuCtxGetId", &f, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            get_id = reinterpret_cast<PfnCtxGetId>(f);
+    });
+    if (!get_current || !get_id) return fail(FME_E_CUDA, "driver entry points cuCtxGetCurrent / cuCtxGetId unavailable");
+    void* ctx = nullptr;
+    if (get_current(&ctx) != 0 || !ctx) return fail(FME_E_CUDA, "no current CUDA context");
+    if (get_id(ctx, id) != 0) return fail(FME_E_CUDA, "cuCtxGetId failed");
+    return FME_OK;
+}
+
 std::mutex g_const_mu;
-bool g_const_done[64];
+unsigned long long g_const_ctx[64];   // context id the constants were uploaded in (0 = none)
 
 std::mutex g_scratch_mu;
 void* g_scratch_addr[64];
+unsigned long long g_scratch_ctx[64];
 
-// Device address of g_raw_scratch on `device`, which must be current: looked up once per device.
+// Device address of g_raw_scratch on `device`, which must be current: looked up once per device and context.
 int static_scratch(int device, uint8_t** out) {
     std::lock_guard<std::mutex> lk(g_scratch_mu);
     if (device < 0 || device >= 64) return fail(FME_E_ARG, "device ordinal out of range");
-    if (!g_scratch_addr[device]) {
+    unsigned long long ctx = 0;
+    int rc = current_context_id(&ctx);
+    if (rc) return rc;
+    if (!g_scratch_addr[device] || g_scratch_ctx[device] != ctx) {
         void* p = nullptr;
         CK(cudaGetSymbolAddress(&p, g_raw_scratch));
         g_scratch_addr[device] = p;
+        g_scratch_ctx[device] = ctx;
     }
     *out = static_cast<uint8_t*>(g_scratch_addr[device]);
     return FME_OK;
@@ -602,7 +654,10 @@ int static_scratch(int device, uint8_t** out) {
 int ensure_constants(int device) {
     std::lock_guard<std::mutex> lk(g_const_mu);
     if (device < 0 || device >= 64) return fail(FME_E_ARG, "device ordinal out of range");
-    if (g_const_done[device]) return FME_OK;
+    unsigned long long ctx = 0;
+    int rc = current_context_id(&ctx);
+    if (rc) return rc;
+    if (g_const_ctx[device] == ctx) return FME_OK;
     uint32_t dt[256];
     build_dtab(dt);
     AreaTabs T;
@@ -624,7 +679,7 @@ int ensure_constants(int device) {
     CK(cudaFuncSetAttribute(k_resize, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
     CK(cudaFuncSetAttribute(k_power, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
     CK(cudaFuncSetAttribute(k_render, cudaFuncAttributeMaxDynamicSharedMemorySize, RB_BYTES));
-    g_const_done[device] = true;
+    g_const_ctx[device] = ctx;
     return FME_OK;
 }
 
@@ -712,11 +767,73 @@ uint64_t sticky_threshold(double sticky) {
 
 constexpr int kChunks = 4;
 constexpr int kTailParts = 4;   // fme_step_to_host renders the last slice in this many parts
-struct HostFix {  // arguments of the host fix-up after fme_step_to_host's copies
+
+// A few persistent host threads for the in-place stack shift of fme_step_to_host (memmove of frames 1..k-1
+// to 0..k-2 in the caller's pinned buffer, as the reference's host engine shifts its stacks,
+// csrc/fastmario.cpp:494-503). Runs inside a stream host function, so it makes no CUDA call.
+class HostPool {
+  public:
+    explicit HostPool(int n) {
+        for (int i = 0; i < n; i++) th_.emplace_back([this, i] { worker(i); });
+    }
+    ~HostPool() {
+        {
+            std::lock_guard<std::mutex> lk(mu_);
+            stop_ = true;
+        }
+        cv_.notify_all();
+        for (auto& t : th_) t.join();
+    }
+    int size() const { return (int)th_.size() + 1; }
+    // fn(part) for part in [0, size()), the calling thread taking the last part; returns when all are done
+    void run(const std::function<void(int)>& fn) {
+        {
+            std::lock_guard<std::mutex> lk(mu_);
+            job_ = &fn;
+            left_ = (int)th_.size();
+            gen_++;
+        }
+        cv_.notify_all();
+        fn((int)th_.size());
+        std::unique_lock<std::mutex> lk(mu_);
+        done_.wait(lk, [this] { return left_ == 0; });
+        job_ = nullptr;
+    }
+
+  private:
+    void worker(int i) {
+        uint64_t seen = 0;
+        for (;;) {
+            const std::function<void(int)>* fn;
+            {
+                std::unique_lock<std::mutex> lk(mu_);
+                cv_.wait(lk, [&] { return stop_ || gen_ != seen; });
+                if (stop_) return;
+                seen = gen_;
+                fn = job_;
+            }
+            (*fn)(i);
+            std::lock_guard<std::mutex> lk(mu_);
+            if (--left_ == 0) done_.notify_one();
+        }
+    }
+    std::vector<std::thread> th_;
+    std::mutex mu_;
+    std::condition_variable cv_, done_;
+    const std::function<void(int)>* job_ = nullptr;
+    int left_ = 0;
+    uint64_t gen_ = 0;
+    bool stop_ = false;
+};
+
+struct HostFix {  // arguments of the host functions of one fme_step_to_host call
     uint8_t* obs = nullptr;
     const uint8_t* term = nullptr;
     const uint8_t* trunc = nullptr;
     int n = 0, K = 0;
+    int e0[kChunks + 1] = {};   // env range of each step slice (in-place shift)
+    int shift_slice = 0;        // slice the next shift host function moves
+    HostPool* pool = nullptr;
 };
 
 struct FmeEnv {
@@ -744,10 +861,15 @@ struct FmeEnv {
     // fme_step_to_host: early copy of the old frames (s_copy, one event per slice) and the host-side fix-up
     cudaStream_t s_copy = nullptr;
     cudaEvent_t ev_pre[kChunks] = {}, ev_copy = nullptr, ev_part[kTailParts] = {};
-    // one argument block per call still in flight (calls enqueued back to back may name other host buffers)
+    // one argument block per call still in flight (calls enqueued back to back may name other host buffers);
+    // a block is reused only after the event recorded behind its call's last host function has completed
     static constexpr int kFixRing = 16;
     HostFix fix[kFixRing] = {};
+    cudaEvent_t fix_done[kFixRing] = {};
     uint32_t fix_next = 0;
+    HostPool* pool = nullptr;
+    // host buffer the last fme_step_to_host wrote the stacks into; cleared by every other step or reset
+    const uint8_t* host_obs_prev = nullptr;
     FmeBuffers buf{};
     bool bound = false;
     uint64_t sticky_thr = 0;
@@ -786,6 +908,9 @@ static void free_env(FmeEnv* v) {
         if (v->ev_pre[c]) cudaEventDestroy(v->ev_pre[c]);
     for (int q = 0; q < kTailParts; q++)
         if (v->ev_part[q]) cudaEventDestroy(v->ev_part[q]);
+    for (int q = 0; q < FmeEnv::kFixRing; q++)
+        if (v->fix_done[q]) cudaEventDestroy(v->fix_done[q]);
+    delete v->pool;
     delete v;
 }
 
@@ -858,6 +983,7 @@ static int create_impl(const FmeConfig* cfg, const uint8_t* rom, int64_t rom_len
         CK(cudaEventCreateWithFlags(&v->ev_copy, cudaEventDisableTiming));
         for (int c = 0; c < v->nch; c++) CK(cudaEventCreateWithFlags(&v->ev_pre[c], cudaEventDisableTiming));
         for (int q = 0; q < kTailParts; q++) CK(cudaEventCreateWithFlags(&v->ev_part[q], cudaEventDisableTiming));
+        for (int q = 0; q < FmeEnv::kFixRing; q++) CK(cudaEventCreateWithFlags(&v->fix_done[q], cudaEventDisableTiming));
         for (int c = 0; c < v->nch; c++) {
             CK(cudaStreamCreateWithPriority(&v->s_emu[c], cudaStreamNonBlocking, hi));
             CK(cudaStreamCreateWithPriority(&v->s_rnd[c], cudaStreamNonBlocking, lo));
@@ -1004,8 +1130,8 @@ static cudaError_t copy_scalars(const StepParams& P, const FmeHostOut* host, int
 }
 
 // fme_step_to_host, after the last copy: an env whose episode ended restarts its stack as K-1 zero frames and
-// the reset frame; the early copy gave it the old frames, so they are cleared here (runs on a driver thread
-// once the copies are done, before the caller's stream moves on).
+// the reset frame; the early copy (or the in-place shift) gave it the old frames, so they are cleared here (runs
+// on a driver thread once the copies are done, before the caller's stream moves on).
 static void CUDART_CB zero_restarted_stacks(void* arg) {
     const HostFix* f = static_cast<const HostFix*>(arg);
     const size_t ob = (size_t)f->K * OBS_BYTES;
@@ -1013,9 +1139,34 @@ static void CUDART_CB zero_restarted_stacks(void* arg) {
         if (f->term[e] | f->trunc[e]) memset(f->obs + (size_t)e * ob, 0, (size_t)(f->K - 1) * OBS_BYTES);
 }
 
+// In-place variant of the early copy: frames 1..K-1 of every stack of the next step slice move to 0..K-2 inside
+// the host buffer, which holds the previous step's stacks. One call per slice, in slice order (stream order on
+// the copy stream); the pool's threads split the slice's envs.
+static void CUDART_CB shift_host_stacks(void* arg) {
+    HostFix* f = static_cast<HostFix*>(arg);
+    const int c = f->shift_slice++;
+    const int a = f->e0[c], b = f->e0[c + 1];
+    const size_t ob = (size_t)f->K * OBS_BYTES, mv = (size_t)(f->K - 1) * OBS_BYTES;
+    uint8_t* obs = f->obs;
+    const int parts = f->pool->size();
+    f->pool->run([=](int q) {
+        const int lo = a + (int)((int64_t)(b - a) * q / parts), hi = a + (int)((int64_t)(b - a) * (q + 1) / parts);
+        for (int e = lo; e < hi; e++) memmove(obs + (size_t)e * ob, obs + (size_t)e * ob + OBS_BYTES, mv);
+    });
+}
+
+static int launch_step_impl(FmeEnv* v, const int64_t* d_actions, void* stream, bool reset, void* mark,
+                            const FmeHostOut* host);
 static int launch_step_like(FmeEnv* v, const int64_t* d_actions, void* stream, bool reset, void* mark = nullptr,
                             const FmeHostOut* host = nullptr) {
     if (!v) return fail(FME_E_ARG, "null env");
+    const int rc = launch_step_impl(v, d_actions, stream, reset, mark, host);
+    // only a complete fme_step_to_host leaves the caller's buffer holding the stacks (for the next in-place call)
+    v->host_obs_prev = (rc == FME_OK && host && !reset) ? host->obs : nullptr;
+    return rc;
+}
+static int launch_step_impl(FmeEnv* v, const int64_t* d_actions, void* stream, bool reset, void* mark,
+                            const FmeHostOut* host) {
     if (!v->bound) return fail(FME_E_STATE, "fme_set_buffers must be called first");
     if (!reset && !d_actions) return fail(FME_E_ARG, "null actions");
     CK(cudaSetDevice(v->cfg.device));
@@ -1036,15 +1187,41 @@ static int launch_step_like(FmeEnv* v, const int64_t* d_actions, void* stream, b
         CK(cudaEventRecord(v->ev_in, s));
         const int K = v->K;
         const size_t ob = (size_t)K * OBS_BYTES;
+        // In place: the caller's buffer holds the stacks the previous call of this env wrote, unchanged.
+        const bool in_place = host && K > 1 && (host->flags & FME_HOST_OBS_IN_PLACE) && v->host_obs_prev == host->obs;
+        HostFix* fx = nullptr;
+        cudaEvent_t fx_done = nullptr;
         if (host && K > 1) {
-            // Frames 1..K-1 of every stack, still untouched on the device, are frames 0..K-2 of the new one: they
-            // go to the host while the envs emulate, leaving only each env's new frame for after its render.
+            const uint32_t slot = v->fix_next++ % FmeEnv::kFixRing;
+            CK(cudaEventSynchronize(v->fix_done[slot]));   // that slot's earlier call has run its host functions
+            fx = &v->fix[slot];
+            fx_done = v->fix_done[slot];
+            fx->obs = host->obs; fx->term = host->term; fx->trunc = host->trunc; fx->n = v->n; fx->K = K;
+            fx->shift_slice = 0;
+            for (int c = 0; c <= v->nch; c++) {
+                const int gc = groups * c / v->nch;
+                fx->e0[c] = gc * 32 < v->n ? gc * 32 : v->n;
+            }
+            if (in_place && !v->pool) {
+                const unsigned hw = std::thread::hardware_concurrency();
+                v->pool = new HostPool((int)std::min(7u, hw > 2 ? hw / 2 : 1u));
+            }
+            fx->pool = v->pool;
+        }
+        if (host && K > 1) {
+            // Frames 1..K-1 of every stack are frames 0..K-2 of the new one. In place they move down inside the
+            // host buffer; otherwise they are copied from the device (still untouched there) while the envs
+            // emulate. Either way only each env's new frame is left for after its render.
             CK(cudaStreamWaitEvent(v->s_copy, v->ev_in, 0));
             for (int c = 0; c < v->nch; c++) {
-                const int g0 = groups * c / v->nch, g1 = groups * (c + 1) / v->nch;
-                const int e0 = g0 * 32, e1 = g1 * 32 < v->n ? g1 * 32 : v->n;
-                CK(cudaMemcpy2DAsync(host->obs + e0 * ob, ob, P.obs + e0 * ob + OBS_BYTES, ob, (size_t)(K - 1) * OBS_BYTES,
-                                     (size_t)(e1 - e0), cudaMemcpyDeviceToHost, v->s_copy));
+                const int e0 = fx->e0[c], e1 = fx->e0[c + 1];
+                if (in_place) {
+                    CK(cudaLaunchHostFunc(v->s_copy, shift_host_stacks, fx));
+                } else {
+                    CK(cudaMemcpy2DAsync(host->obs + e0 * ob, ob, P.obs + e0 * ob + OBS_BYTES, ob,
+                                         (size_t)(K - 1) * OBS_BYTES, (size_t)(e1 - e0), cudaMemcpyDeviceToHost,
+                                         v->s_copy));
+                }
                 CK(cudaEventRecord(v->ev_pre[c], v->s_copy));
             }
         }
@@ -1056,7 +1233,8 @@ static int launch_step_like(FmeEnv* v, const int64_t* d_actions, void* stream, b
             k_step<true><<<g1 - g0, 32, STEP_SMEM, v->s_emu[c]>>>(P);
             CK(cudaEventRecord(v->ev_emu[c], v->s_emu[c]));
             CK(cudaStreamWaitEvent(v->s_rnd[c], v->ev_emu[c], 0));
-            if (host && K > 1) CK(cudaStreamWaitEvent(v->s_rnd[c], v->ev_pre[c], 0));  // old frames copied first
+            // the device copy of the old frames must read them before the render moves them
+            if (host && K > 1 && !in_place) CK(cudaStreamWaitEvent(v->s_rnd[c], v->ev_pre[c], 0));
             if (host && K > 1 && v->nch > 1 && c == v->nch - 1) {
                 // the last slice's copies are the ones nothing hides: its scalars go as soon as it has emulated,
                 // and it is rendered in parts, each part's new frames copied while the next part renders
@@ -1081,6 +1259,8 @@ static int launch_step_like(FmeEnv* v, const int64_t* d_actions, void* stream, b
             if (host) {  // this slice's outputs to the host while later slices still run
                 const size_t ne = (size_t)(e1 - e0), fo = (size_t)(K - 1) * OBS_BYTES;
                 cudaStream_t cs = v->s_rnd[c];
+                // in place, the shift reads host frame K-1 before the new frame lands there
+                if (in_place) CK(cudaStreamWaitEvent(cs, v->ev_pre[c], 0));
                 CK(cudaMemcpy2DAsync(host->obs + e0 * ob + fo, ob, P.obs + e0 * ob + fo, ob, OBS_BYTES, ne,
                                      cudaMemcpyDeviceToHost, cs));
                 CK(copy_scalars(P, host, e0, ne, cs));
@@ -1093,9 +1273,8 @@ static int launch_step_like(FmeEnv* v, const int64_t* d_actions, void* stream, b
         }
         if (host && K > 1) {
             for (int c = 0; c < v->nch; c++) CK(cudaStreamWaitEvent(v->s_copy, v->ev_rnd[c], 0));
-            HostFix* fx = &v->fix[v->fix_next++ % FmeEnv::kFixRing];
-            fx->obs = host->obs; fx->term = host->term; fx->trunc = host->trunc; fx->n = v->n; fx->K = K;
             CK(cudaLaunchHostFunc(v->s_copy, zero_restarted_stacks, fx));
+            CK(cudaEventRecord(fx_done, v->s_copy));
             CK(cudaEventRecord(v->ev_copy, v->s_copy));
             CK(cudaStreamWaitEvent(s, v->ev_copy, 0));
         }
@@ -1161,6 +1340,11 @@ int fme_frames(FmeEnv* v, int64_t* out) {
 int fme_bad_ops(FmeEnv* v, int64_t* out) {
     if (!v || !out) return fail(FME_E_ARG, "null env / out");
     return sum_words(v, S_BADOPS, -1, out);
+}
+int fme_work_counters(FmeEnv* v, int64_t* instructions, int64_t* frames) {
+    if (!v || !instructions || !frames) return fail(FME_E_ARG, "null env / out");
+    int rc = sum_words(v, S_INSTR_LO, S_INSTR_HI, instructions);
+    return rc ? rc : sum_words(v, S_EMU_FRAMES, -1, frames);
 }
 int64_t fme_env_bytes(FmeEnv* v) {
     if (!v) return -1;
@@ -1366,6 +1550,7 @@ int fme_resize(const uint8_t* d_src, uint8_t* d_dst, int32_t n, void* stream) {
     if (!d_src || !d_dst || n < 0) return fail(FME_E_ARG, "bad resize arguments");
     int dev = 0;
     CK(cudaGetDevice(&dev));
+    CK(cudaSetDevice(dev));  // makes the device's primary context current (ensure_constants keys on it)
     int rc = ensure_constants(dev);
     if (rc) return rc;
     if (n == 0) return FME_OK;

@@ -163,6 +163,9 @@ enum Scal : int {
     S_RNG_I0, S_RNG_I1, S_RNG_I2, S_RNG_I3,  // PCG64 increment
     S_RNG_HAS, S_RNG_U32,                    // numpy has_uint32 / uinteger
     S_LEVEL, S_FRAMES_LO, S_FRAMES_HI, S_BADOPS, S_STATUS,
+    // emulated-work counters of the timed step kernel (not part of the env semantics): 6502 instructions
+    // executed (the idle-loop fast-forward and the sprite-0 poll skip count none) and NES frames run
+    S_INSTR_LO, S_INSTR_HI, S_EMU_FRAMES,
     S_WORDS
 };
 // register flag byte inside S_PPU2 (bits 16-23)

@@ -18,6 +18,7 @@ struct Hot {
     int32_t exec_at, thresh;
     uint32_t zero_skip, bad;
     uint32_t ux, uy;  // micro-op of the instruction at pc (fme_defs.h); zero outside PRG
+    uint32_t icount;  // instructions executed since hot_init (emulated-work counter)
 };
 
 // Exact slow paths (the Core methods), out of line so the hot loop stays small.
@@ -331,6 +332,7 @@ FME_HD bool hot_step(Hot& h, Core& c, const Fast& f) {
     }
     h.exec_at = J + (S >= 1 ? S : 1);
     h.zero_skip = S <= 0 ? 1u : 0u;
+    h.icount++;
     return true;
 }
 

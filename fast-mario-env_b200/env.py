@@ -182,6 +182,13 @@ class CudaVecEnv:
         N.check(N.lib().fme_bad_ops(self.h, ctypes.byref(v)), "fme_bad_ops")
         return int(v.value)
 
+    def work_counters(self) -> tuple[int, int]:
+        """(6502 instructions executed, NES frames run) by all envs' steps so far (fme_work_counters)."""
+        _torch().cuda.synchronize(self.dev)
+        i, f = ctypes.c_int64(), ctypes.c_int64()
+        N.check(N.lib().fme_work_counters(self.h, ctypes.byref(i), ctypes.byref(f)), "fme_work_counters")
+        return int(i.value), int(f.value)
+
     def bytes_per_env(self) -> float:
         own = int(N.lib().fme_env_bytes(self.h))
         outs = sum(t.numel() * t.element_size() for t in (self.obs, self.final_obs, self.rew, self.term, self.trunc,
@@ -200,23 +207,37 @@ class CudaVecEnv:
             pass
 
 
+def _monitor_file(path: str) -> str:
+    """Where a monitor writes: an existing directory gets monitor.monitor.csv inside it, any other path gains the
+    .monitor.csv suffix unless it already ends with it (the file name SB3's load_results looks for)."""
+    suffix = ".monitor.csv"
+    if path.endswith(suffix):
+        return path
+    return os.path.join(path, "monitor" + suffix) if os.path.isdir(path) else path + suffix
+
+
 class MonitorCSV:
-    """SB3 VecMonitor-compatible monitor.monitor.csv (columns r,l,t,x_pos,flag_get), as env.py:93-110."""
+    """Episode log in SB3's VecMonitor CSV format, written as the reference FastVecEnv writes it
+    (src/fast_mario_env/env.py:93-110): a '#'-prefixed JSON line (t_start, env_id), the header
+    r,l,t,x_pos,flag_get, then one row per finished episode, flushed at once so a crash loses nothing."""
+
+    COLUMNS = ("r", "l", "t", "x_pos", "flag_get")
 
     def __init__(self, path: str):
-        if not path.endswith(".monitor.csv"):
-            path = os.path.join(path, "monitor.monitor.csv") if os.path.isdir(path) else path + ".monitor.csv"
-        os.makedirs(os.path.dirname(os.path.abspath(path)), exist_ok=True)
-        self.f = open(path, "w")
-        self.f.write("#%s\n" % json.dumps({"t_start": time.time(), "env_id": "None"}))
-        self.f.write("r,l,t,x_pos,flag_get\n")
+        target = _monitor_file(path)
+        os.makedirs(os.path.dirname(os.path.abspath(target)), exist_ok=True)
+        self.f = open(target, "w")
+        self._emit("#" + json.dumps({"t_start": time.time(), "env_id": "None"}))
+        self._emit(",".join(self.COLUMNS))
+
+    def _emit(self, line: str) -> None:
+        self.f.write(line + "\n")
         self.f.flush()
 
-    def write(self, e: dict):
-        self.f.write(f"{e['r']},{e['l']},{e['t']},{e['x_pos']},{e['flag_get']}\n")
-        self.f.flush()
+    def write(self, episode: dict) -> None:
+        self._emit(",".join(str(episode[c]) for c in self.COLUMNS))
 
-    def close(self):
+    def close(self) -> None:
         self.f.close()
 
 
@@ -249,8 +270,9 @@ class FastVecEnv:
         self._epr = torch.zeros(n_envs, dtype=torch.float64, **pin)
         self._epl = torch.zeros(n_envs, dtype=torch.int32, **pin)
         self._event = torch.cuda.Event()
+        # the pinned obs buffer always holds the stacks of the last step, so the library shifts it in place
         self._hout = N.FmeHostOut(*[t.data_ptr() for t in (self._obs, self._rew, self._term, self._trunc, self._info,
-                                                            self._epr, self._epl)])
+                                                            self._epr, self._epl)], N.FME_HOST_OBS_IN_PLACE)
         self.monitor = MonitorCSV(monitor_path) if monitor_path else None
         self.t0 = time.time()
         self._pending = False

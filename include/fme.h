@@ -103,6 +103,7 @@ int fme_step(FmeEnv* env, const int64_t* d_actions, void* stream);
 int fme_step_marked(FmeEnv* env, const int64_t* d_actions, void* stream, void* event);
 
 /* Pinned host destinations of fme_step_to_host (shapes as FmeBuffers; final_obs stays on the device). */
+#define FME_HOST_OBS_IN_PLACE 1u   /* FmeHostOut.flags: obs holds this env's previous stacks (see below) */
 typedef struct FmeHostOut {
     uint8_t* obs;
     float* rew;
@@ -111,13 +112,19 @@ typedef struct FmeHostOut {
     int32_t* info;
     double* ep_ret;
     int32_t* ep_len;
+    uint32_t flags;   /* FME_HOST_OBS_IN_PLACE or 0 */
 } FmeHostOut;
-/* fme_step, and the step's outputs copied into pinned host memory while the step runs: frames 1..k-1 of every
- * stack (frames 0..k-2 of the new one) as soon as the step starts, each slice's new frames and scalars once
- * that slice's kernels are done (the last slice rendered and copied in parts), and, last, a host function (cudaLaunchHostFunc) clears frames 0..k-2 of the
- * envs whose episode ended (their stack restarts as zeros + the reset frame). Replaces fm_step_async +
- * fm_step_wait's host-buffer outputs (csrc/fastmario.cpp:611-617) for callers that want host arrays. Async:
- * synchronise the stream before reading `out`; at most 16 calls of one env may be in flight at once. */
+/* fme_step, and the step's outputs copied into pinned host memory while the step runs. Frames 1..k-1 of every
+ * stack are frames 0..k-2 of the new one: with FME_HOST_OBS_IN_PLACE, when `obs` is the buffer this env's
+ * previous fme_step_to_host filled (and the caller has not changed it since; no fme_step or fme_reset of the
+ * env came in between), they move down inside that host buffer (host threads, as the reference's host engine
+ * shifts its stacks in place, csrc/fastmario.cpp:494-503); otherwise they are copied from the device as soon
+ * as the step starts. Then each slice's new frames and scalars go to the host once that slice's kernels are
+ * done (the last slice rendered and copied in parts), and, last, a host function (cudaLaunchHostFunc) clears
+ * frames 0..k-2 of the envs whose episode ended (their stack restarts as zeros + the reset frame). Replaces
+ * fm_step_async + fm_step_wait's host-buffer outputs (csrc/fastmario.cpp:611-617) for callers that want host
+ * arrays. Async: synchronise the stream before reading `out`. Up to 16 calls of one env may be in flight; a
+ * 17th waits (on the host) until the oldest one's host functions have run. */
 int fme_step_to_host(FmeEnv* env, const int64_t* d_actions, const FmeHostOut* out, void* stream);
 
 /* OR of the device status bits of all envs since create (call after synchronising). */
@@ -132,6 +139,12 @@ int fme_ram_all(FmeEnv* env, uint8_t* d_out, void* stream);
  * Replace fm_frames / fm_bad_ops (csrc/fastmario.cpp:619-628). */
 int fme_frames(FmeEnv* env, int64_t* out);
 int fme_bad_ops(FmeEnv* env, int64_t* out);
+/* Emulated work of the steps so far, summed over all envs (synchronous): 6502 instructions executed (the
+ * idle-loop fast-forward and the sprite-0 poll skip execute none) and NES frames actually run by the step
+ * kernel (unlike fme_frames, without the frames of no-op starts served from the reset cache or of the
+ * early-termination frames the reference re-emulates). No counterpart in the reference; the reference quotes
+ * emulated instructions per agent step in its documentation (README.md:261-262). */
+int fme_work_counters(FmeEnv* env, int64_t* instructions, int64_t* frames);
 /* Device bytes held per env (replaces fm_env_bytes, csrc/fastmario.cpp:632-635). */
 int64_t fme_env_bytes(FmeEnv* env);
 
@@ -164,7 +177,9 @@ void fme_raw_destroy(FmeRaw* raw);
  * frame rewrites its slot header before the records it reads back. The first call on a device looks the
  * array's address up (cudaGetSymbolAddress) with that device current; make it before any stream capture.
  * All calls on one device share the array, so calls that can overlap (other streams, other threads)
- * race and must be ordered by the caller. Async. */
+ * race and must be ordered by the caller. The screens go only to d_screens: the handle's own screen buffer
+ * is not written, so fme_raw_screen keeps returning the screens of the last fme_raw_frame call. The array's
+ * address is looked up again in a new CUDA context (after a cudaDeviceReset, for example). Async. */
 #define FME_STATIC_MAX_CONSOLES 64
 #define FME_STATIC_LOG_CAPACITY 2048
 int fme_raw_frame_static(FmeRaw* raw, const uint8_t* d_buttons, uint8_t* d_screens, int32_t render,

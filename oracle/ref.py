@@ -174,13 +174,18 @@ class RefVecEnv:
     """
 
     def __init__(self, rom: bytes, levels, n: int, seed=0, skip=4, max_steps=2000, sticky=0.0, noop_max=0,
-                 maxpool=False, frame_stack=4, n_threads=0, env_offset=0):
+                 maxpool=False, frame_stack=4, n_threads=0, env_offset=0, env_ids=None):
+        """env_ids: global indices of the n envs of a larger run (any order, not necessarily contiguous); env k
+        is then seeded as env env_ids[k] of that run, default_rng(seed*1000 + env_ids[k]). Without it the envs
+        are env_offset .. env_offset + n - 1, as in the reference."""
         L = lib()
         self.n, self.k = n, frame_stack
         lv = np.array([tuple(levels)] * n if isinstance(levels[0], int) else list(levels), np.int32).reshape(-1)
         assert lv.size == 3 * n
         self._lv = lv
-        self._rng = np.array([rng_state(seed * 1000 + env_offset + i) for i in range(n)], np.uint64).reshape(-1)
+        ids = [env_offset + i for i in range(n)] if env_ids is None else [int(i) for i in env_ids]
+        assert len(ids) == n
+        self._rng = np.array([rng_state(seed * 1000 + i) for i in ids], np.uint64).reshape(-1)
         self._rom = np.frombuffer(rom, np.uint8).copy()
         self._lut = gray_lut()
         self.h = L.fm_create(_ptr(self._rom), len(self._rom), n, _ptr(self._lv), _ptr(self._lut), skip, max_steps,

@@ -66,11 +66,16 @@ def pytest_collection_modifyitems(config, items):
             item.add_marker(skip)
 
 
-@pytest.fixture(scope="session")
-def oracle():
+@pytest.fixture
+def oracle(request):
+    """The reference's own C++ core (oracle/_ref/libfastmario.so). A GPU parity test without it fails: a parity
+    suite that turned into skips would pass while checking nothing. CPU-only tests skip instead."""
     import ref
     if not ref.available():
-        pytest.skip("reference oracle not built (make -C oracle ref)")
+        msg = "reference oracle not built (make -C oracle REF=<reference checkout>)"
+        if request.node.get_closest_marker("gpu") is not None:
+            pytest.fail(msg)
+        pytest.skip(msg)
     return ref
 
 

@@ -95,7 +95,7 @@ void hr_frame(void* h, const uint8_t* buttons) {
         uint8_t* slot = r->log.data();
         begin_frame(c, slot, buttons[e], kLogCap);
         const Fast fst{c.ram, r->prg.data(), reinterpret_cast<const uint32_t*>(r->prg.data() + 0x8000)};
-        Hot hot;
+        Hot hot{};
         hot_in(hot, c, fst);
         while (hot_step(hot, c, fst)) {
         }

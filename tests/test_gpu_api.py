@@ -160,6 +160,55 @@ def test_step_to_host_back_to_back_with_two_buffer_sets(rom):
     h.close(); d.close()
 
 
+def test_step_to_host_in_place_shift_many_calls_in_flight(rom):
+    """FME_HOST_OBS_IN_PLACE: 20 fme_step_to_host calls into one pinned buffer set, enqueued without a sync
+    (more than the 16 argument blocks, so later calls wait for earlier ones' host functions); the host stacks
+    are shifted in place by the library. Then calls alternating between two buffer sets with the flag set, which
+    must fall back to copying the old frames from the device. Each is checked against fme_step's device buffers."""
+    import ctypes
+    import torch
+    from fast_mario_env_b200 import _native as N
+    levels = ["1-1", "3-2", "5-4", "8-1", "2-2"] * 30
+    kw = dict(seed=31, sticky=0.25, noop_max=30, maxpool=True, max_steps=12, rom=rom)
+    h = fme.CudaVecEnv(levels, 150, **kw)
+    d = fme.CudaVecEnv(levels, 150, **kw)
+    h.reset()
+    d.reset()
+    pin = dict(pin_memory=True)
+
+    def bufs():
+        t = (torch.zeros(150, 4, 84, 84, dtype=torch.uint8, **pin), torch.zeros(150, dtype=torch.float32, **pin),
+             torch.zeros(150, dtype=torch.bool, **pin), torch.zeros(150, dtype=torch.bool, **pin),
+             torch.zeros(150, len(fme.INFO_FIELDS), dtype=torch.int32, **pin),
+             torch.zeros(150, dtype=torch.float64, **pin), torch.zeros(150, dtype=torch.int32, **pin))
+        return t, N.FmeHostOut(*[x.data_ptr() for x in t], N.FME_HOST_OBS_IN_PLACE)
+
+    (ta, oa), (tb, ob) = bufs(), bufs()
+    ta[0].copy_(h.obs.cpu())   # the reset stacks (reset is device-only, so the first call copies anyway)
+    rng = np.random.default_rng(32)
+    acts = [torch.from_numpy(rng.integers(0, 7, 150)).cuda() for _ in range(20)]
+    ended = 0
+    for a in acts:
+        h.actions.copy_(a)
+        N.check(N.lib().fme_step_to_host(h.h, N.ptr(h.actions), ctypes.byref(oa), h._stream()), "step_to_host")
+    torch.cuda.synchronize()
+    for a in acts:
+        o, r, te, tr, _ = d.step(a)
+        ended += int((te | tr).sum())
+    assert torch.equal(ta[0], o.cpu()) and torch.equal(ta[1], r.cpu())
+    assert torch.equal(ta[4], d.info_t.cpu())
+    assert ended > 50
+    for k in range(6):   # alternating buffers: never the buffer the previous call wrote, so no in-place shift
+        a = torch.from_numpy(rng.integers(0, 7, 150)).cuda()
+        t, o_ = (tb, ob) if k % 2 == 0 else (ta, oa)
+        h.actions.copy_(a)
+        N.check(N.lib().fme_step_to_host(h.h, N.ptr(h.actions), ctypes.byref(o_), h._stream()), "step_to_host")
+        torch.cuda.synchronize()
+        o, r, te, tr, _ = d.step(a)
+        assert torch.equal(t[0], o.cpu()) and torch.equal(t[1], r.cpu()), k
+    h.close(); d.close()
+
+
 def test_resize_matches_cv2_golden():
     g = np.load(os.path.join(GOLD, "resize.npz"))
     out = fme.resize_area(g["src"])

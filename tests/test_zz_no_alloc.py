@@ -45,6 +45,35 @@ def test_static_frame_matches_raw_frame_on_two_calls_in_a_row(rom_div):
     b.close()
 
 
+def test_static_frame_with_the_full_array_and_untouched_handle_screens(rom_div):
+    """64 consoles, every slot of the array, rendering on two calls in a row; the handle's own screen buffer
+    keeps the screens of its last fme_raw_frame."""
+    import torch
+    n = N.FME_STATIC_MAX_CONSOLES
+    a = fme.RawNESBatch(rom_div, n)
+    b = fme.RawNESBatch(rom_div, n)
+    rng = np.random.default_rng(64)
+    for f in range(LEAD_FRAMES):
+        btn = rng.integers(0, 256, n).astype(np.uint8)
+        a.frame(btn, f == LEAD_FRAMES - 1)
+        b.frame(btn, f == LEAD_FRAMES - 1)
+    before = b.screen().cpu().numpy()
+    scr = torch.zeros((n, 240, 256), dtype=torch.uint8, device=b.dev)
+    for call in range(2):
+        btn = torch.as_tensor(rng.integers(0, 256, n).astype(np.uint8)).to(b.dev)
+        a.frame(btn, True)
+        N.check(N.lib().fme_raw_frame_static(b.h, N.ptr(btn), N.ptr(scr), 1, _stream(b)), "fme_raw_frame_static")
+        want = a.screen().cpu().numpy()
+        assert not np.array_equal(want, before), "the compared frames did not change the screens"
+        assert np.array_equal(scr.cpu().numpy(), want), f"screens differ on call {call}"
+        assert np.array_equal(b.ram().cpu().numpy(), a.ram().cpu().numpy()), f"RAM differs on call {call}"
+    assert np.array_equal(b.screen().cpu().numpy(), before), "fme_raw_screen changed after static calls"
+    a.check()
+    b.check()
+    a.close()
+    b.close()
+
+
 def test_static_frame_without_render_takes_no_screen_buffer(rom):
     import torch
     a = fme.RawNESBatch(rom, 3)

@@ -258,6 +258,8 @@ def run_ppo(args, rank, world, dev, dist):
         coll += c0.elapsed_time(c1)
     e1.record()
     torch.cuda.synchronize(dev)
+    if bool(tr.trunc_overflow):
+        raise RuntimeError("time-limit truncations exceeded PPOConfig.trunc_budget in a rollout step")
     ms = e0.elapsed_time(e1)
     ms_max = shard.max_over_ranks(ms, device=dev)
     samples = world * E * cfg.n_steps * iters
@@ -268,7 +270,12 @@ def run_ppo(args, rank, world, dev, dist):
                           "dtype": "fp32", "data": "synthetic",
                           "config": {"workload": "config4: Nature-CNN PPO on config-1 envs", "n_envs_per_gpu": E,
                                      "n_steps": 128, "epochs": 4, "minibatch": 1024, "gamma": 0.99, "lam": 0.95,
-                                     "parallelism": f"dp{world} (NCCL gradient all-reduce)" if world > 1 else "dp1"}}))
+                                     "parallelism": f"dp{world} (NCCL gradient all-reduce inside the captured "
+                                                    "minibatch graph)" if world > 1 else "dp1"}}))
+    tr.L.graph = None   # graphs holding NCCL calls are released before the process group is destroyed
+    tr.pgraph = None
+    del tr
+    torch.cuda.synchronize(dev)
     env.close()
 
 

@@ -39,6 +39,7 @@ class PPOConfig:
     max_grad_norm: float = 0.5
     graph: bool = True
     channels_last: bool = True   # NHWC activations and weights for the convolutions (the reference's default)
+    trunc_budget: int = 64       # time-limit truncations bootstrapped per rollout step without a host sync
 
 
 class NatureAC(nn.Module):
@@ -146,7 +147,8 @@ class Storage:
 
 class Learner:
     """GAE + epochs x shuffled minibatches (train.py:112-247). With a process group of world size > 1 the
-    gradients are averaged over ranks (NCCL all-reduce of one flat buffer) before clipping."""
+    gradients are averaged over ranks (NCCL all-reduce of one flat buffer) before clipping, inside the captured
+    minibatch graph."""
 
     def __init__(self, cfg: PPOConfig, dev, net: NatureAC | None = None):
         self.cfg, self.dev = cfg, dev
@@ -203,10 +205,10 @@ class Learner:
         self._apply(st)
 
     def _capture(self):
-        """One graph for the minibatch step (single rank), captured on dummy indices; parameters and Adam state
-        are restored afterwards. With several ranks the step runs eagerly around the NCCL all-reduce."""
-        if self.world > 1:
-            return
+        """One graph for the minibatch step, captured on dummy indices; parameters and Adam state are restored
+        afterwards. With several ranks the NCCL all-reduce of the gradients is part of the graph (every rank
+        captures, and later replays, the same collective in the same order); the eager warm-up steps before
+        the capture set up the communicator."""
         snap = [p.detach().clone() for p in self.params]
         self.mb_idx.copy_(torch.randint(0, self.cfg.n_steps * self.cfg.n_envs, (self.cfg.batch,), device=self.dev))
         s = torch.cuda.Stream(self.dev)
@@ -259,6 +261,8 @@ class Trainer:
         self.inp = torch.zeros((cfg.n_envs, 4, 84, 84), dtype=torch.uint8, device=dev)
         self.a = torch.zeros(cfg.n_envs, dtype=torch.int64, device=dev)
         self.lp, self.v = torch.zeros(cfg.n_envs, device=dev), torch.zeros(cfg.n_envs, device=dev)
+        # set on the device when a rollout step had more truncations than cfg.trunc_budget (checked per iteration)
+        self.trunc_overflow = torch.zeros((), dtype=torch.bool, device=dev)
         self.pgraph = None
         if cfg.graph:
             s = torch.cuda.Stream(dev)
@@ -289,17 +293,32 @@ class Trainer:
             b.rew[t].copy_(rew)
             d = (term | trunc).float()
             (b.done[t + 1] if t + 1 < c.n_steps else b.next_done).copy_(d)
-            tmask = trunc & ~term
-            if bool(tmask.any()):  # rare (time limit): one small sync
-                ti = tmask.nonzero().squeeze(-1)
-                with torch.no_grad():
-                    _, v = self.L.net(info["final_obs"][ti], c.channels_last)
-                b.rew[t, ti] += c.gamma * v
+            self._bootstrap_truncations(t, trunc & ~term, info["final_obs"])
         self.obs = self.inp
         with torch.no_grad():
             _, nv = self.L.net(self.inp, c.channels_last)
         b.next_val.copy_(nv)
 
+    def _bootstrap_truncations(self, t, tmask, final_obs):
+        """SB3's time-limit bootstrap (train.py:416-421): r[t, i] += gamma * V(final_obs[i]) for the envs cut off
+        by the time limit, without a host sync. A fixed number (trunc_budget) of such envs is gathered each step
+        (torch.nonzero_static, padded with an out-of-range index whose contribution is masked to zero); a step
+        with more sets trunc_overflow, which iterate() turns into an error rather than a silently missing
+        bootstrap."""
+        c, b = self.cfg, self.L.buf
+        n = c.n_envs
+        ti = torch.nonzero_static(tmask, size=c.trunc_budget, fill_value=n).squeeze(-1)
+        valid = ti < n
+        ti = ti.clamp(max=n - 1)
+        with torch.no_grad():
+            _, v = self.L.net(final_obs.index_select(0, ti), c.channels_last)
+        b.rew[t].index_add_(0, ti, torch.where(valid, c.gamma * v, torch.zeros_like(v)))
+        self.trunc_overflow |= tmask.sum() > c.trunc_budget
+
     def iterate(self):
         self.collect()
-        return self.L.update()
+        stats = self.L.update()
+        if bool(self.trunc_overflow):
+            raise RuntimeError(f"a rollout step had more than trunc_budget={self.cfg.trunc_budget} time-limit "
+                               "truncations; raise PPOConfig.trunc_budget")
+        return stats

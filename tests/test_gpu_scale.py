@@ -14,12 +14,15 @@ Every step compares, for every env of the slices: the stacked observation, rewar
 the ten info fields; for envs whose episode ended also final_obs, episode return and length; every 50 steps
 the 2 KB RAM. Uniform random actions over 7 from a host generator.
 
-With the seed-0 image and random actions an episode lasts about 220 agent steps (most end by a death or the
-flag long before the 2,000-step time limit), so a fixed slice almost never reaches the time limit. Envs still
-in their first episode after 1,500 steps therefore join the comparison then: the oracle replays their 1,500
-recorded actions, the engine's observation and RAM of those envs must equal the oracle's at that point, and
-both are compared in lockstep from there on, so every env of the run that reaches the 2,000-step truncation in
-its first episode is compared at that step.
+With the seed-0 image and uniform random actions an episode lasts about 220 agent steps and never past about
+900: the "right" actions carry every env to the flag (x_pos 3072) long before the 2,000-step time limit. In
+the config-1 run the odd envs therefore draw their actions from {NOOP, A, left} only ("stay-behind" envs:
+they never reach the flag, so only the game's random deaths end their episodes and a few of them reach the
+time limit), the even envs uniformly from all 7 as config 1 states. Envs still in their first episode after
+1,500 steps join the comparison then: the oracle replays their 1,500 recorded actions, the engine's
+observation and RAM of those envs must equal the oracle's at that point, and both are compared in lockstep
+from there on, so every env of the run that reaches the 2,000-step truncation in its first episode is compared
+at that step.
 
 Length: 2,500 steps; FME_TEST_SCALE=4 gives the 10,000 steps of BASELINE config 1.
 """
@@ -80,7 +83,10 @@ def _gather(env, idx, with_ram):
     return got, ram
 
 
-def _run(oracle, rom, n, slices, kw, steps, action_seed):
+STAY_BEHIND = np.array([0, 5, 6])   # NOOP, A, left: no action moves right
+
+
+def _run(oracle, rom, n, slices, kw, steps, action_seed, stay_behind=False):
     import torch
     levels = level_names(n)
     env = fme.CudaVecEnv(levels, n, seed=0, rom=rom, **kw)
@@ -95,8 +101,11 @@ def _run(oracle, rom, n, slices, kw, steps, action_seed):
     first_ep = np.ones(n, bool)          # still in the episode that started at reset()
     late = None
     stats = dict(episodes=0, truncations=0, run_truncations=0, first_episode_truncations=0, joined=0)
+    odd = np.arange(n) % 2 == 1
     for t in range(steps):
         a = rng.integers(0, 7, n)
+        if stay_behind:
+            a[odd] = STAY_BEHIND[a[odd] % 3]
         if t < JOIN_AT:
             history[t] = a
         env.step(torch.from_numpy(a).to(dev))
@@ -134,13 +143,15 @@ def _run(oracle, rom, n, slices, kw, steps, action_seed):
 
 def test_config1_32768_envs_lockstep_slices(oracle, rom):
     kw = dict(sticky=0.25, noop_max=30, maxpool=True, max_steps=2000, skip=4, frame_stack=4)
-    stats = _run(oracle, rom, 32768, [(0, 128), (16384, 16512), (32640, 32768)], kw, scaled(2500), action_seed=2500)
+    stats = _run(oracle, rom, 32768, [(0, 128), (16384, 16512), (32640, 32768)], kw, scaled(2500), action_seed=2500,
+                 stay_behind=True)
     print("config1 32768 envs:", stats)
     assert stats["episodes"] > 0
     # the time limit: every env of the run that lasted 2,000 steps in its first episode joined the comparison
     # at step 1,500 and was compared when it truncated
-    if stats["joined"] < JOIN_MAX:
-        assert stats["truncations"] >= stats["first_episode_truncations"]
+    assert stats["first_episode_truncations"] > 0, "no env reached the 2,000-step time limit"
+    assert stats["joined"] < JOIN_MAX
+    assert stats["truncations"] >= stats["first_episode_truncations"]
 
 
 def test_config2_divergent_4096_envs_lockstep_slices(oracle, rom_div):

@@ -185,25 +185,48 @@ __global__ void __launch_bounds__(32, 1) k_step(StepParams P) {
     Agent ag;
     bool running = active;
     if (active) ag.start(c, ev, cfg, act, d.logs + slot_off(e, 0, cap), d.logs + slot_off(e, 1, cap));
-    // one emulated instruction per lane per iteration; the vote keeps the warp converged at the loop head
+    // Two phases. (1) Every lane whose next instruction the datapath can run executes it, each lane its own
+    // instruction (fme_dp.h): no vote, all lanes at once. (2) When no lane can, the warp votes for its
+    // minimum key and those lanes take one step on the exact path (I/O, PPU catch-up and NMI, the idle-loop
+    // fast-forward, the frame end), all lanes at that PC together. Lanes are independent, so the order in
+    // which the warp serves them changes no result.
     const Fast fst{c.ram, d.prg, d.uop};
     const uint32_t ip0 = __ldg(d.uop + UOP_WORDS), ip1 = __ldg(d.uop + UOP_WORDS + 1);
     Hot h;
     h.icount = 0;
     uint32_t emu_frames = 0;
     hot_in(h, c, fst);
+    rf_pack(h);
+    dfetch(h, d.dop);
+    bool blocked = false;   // a computed address of the lane's next instruction is an I/O address
+    int32_t lim = dp_limit(h);
     for (;;) {
+        const bool ready = running && !blocked && dp_ready(h, lim);
+        if (__any_sync(FULL, ready)) {
+            const bool done = dp_exec(h, fst, d.dop, ready);   // all lanes run the code, ready ones commit
+            blocked = blocked || (ready && !done);
+            continue;
+        }
         const uint32_t key = sched_key_pc(running, h, ip0, ip1);
         const uint32_t mn = __reduce_min_sync(FULL, key);
         if (mn == 0xffffffffu) break;
-        if (key == mn && !hot_step(h, c, fst)) {
-            hot_out(h, c);
-            c.end_frame();
-            emu_frames++;
-            running = ag.on_frame_end(c, ev, cfg);
-            hot_in(h, c, fst);
+        if (key == mn) {
+            rf_unpack(h);
+            fetch(h, fst);   // the exact path's micro-op of pc
+            if (!hot_step(h, c, fst)) {
+                hot_out(h, c);
+                c.end_frame();
+                emu_frames++;
+                running = ag.on_frame_end(c, ev, cfg);
+                hot_in(h, c, fst);
+            }
+            rf_pack(h);
+            dfetch(h, d.dop);
+            lim = dp_limit(h);
+            blocked = false;
         }
     }
+    rf_unpack(h);
     hot_out(h, c);
 
     int reset_ci = 0;
@@ -729,19 +752,24 @@ struct DevBufs {  // one set of per-env state buffers
     }
 };
 
-// The PRG image and its micro-op table share one allocation: 32 KB of PRG, then 2 words per PRG address.
+// The PRG image and its micro-op tables share one allocation: 32 KB of PRG, then 2 words per PRG address of
+// exact micro-ops (+ the first two idle-loop PCs), then 2 words per PRG address of datapath micro-ops.
 constexpr size_t PRG_UOP_OFF = 0x8000;
-constexpr size_t PRG_ALLOC = PRG_UOP_OFF + (size_t)(UOP_WORDS + 2) * 4;  // + the first two idle-loop PCs
+constexpr size_t PRG_DOP_OFF = PRG_UOP_OFF + (size_t)(UOP_WORDS + 2) * 4;
+constexpr size_t PRG_ALLOC = PRG_DOP_OFF + (size_t)UOP_WORDS * 4;
+static_assert(PRG_DOP_OFF % 8 == 0, "datapath micro-ops are read as 8-byte words");
 cudaError_t upload_prg(uint8_t* d_prg, const std::vector<uint8_t>& prg) {
     uint32_t dt[256];
     build_dtab(dt);
-    std::vector<uint32_t> uops(UOP_WORDS + 2);
+    std::vector<uint32_t> uops(UOP_WORDS + 2), dops(UOP_WORDS);
     build_uops(prg.data(), dt, uops.data());
+    build_dops(uops.data(), dops.data());
     uops[UOP_WORDS] = uops[UOP_WORDS + 1] = 0xffffffffu;  // no such pc
     for (uint32_t i = 0, k = 0; i < 0x8000u && k < 2; i++)
         if (uops[2 * i] & UOP_IDLE) uops[UOP_WORDS + k++] = 0x8000u + i;
     cudaError_t e = cudaMemcpy(d_prg, prg.data(), 0x8000, cudaMemcpyHostToDevice);
     if (e == cudaSuccess) e = cudaMemcpy(d_prg + PRG_UOP_OFF, uops.data(), (size_t)(UOP_WORDS + 2) * 4, cudaMemcpyHostToDevice);
+    if (e == cudaSuccess) e = cudaMemcpy(d_prg + PRG_DOP_OFF, dops.data(), (size_t)UOP_WORDS * 4, cudaMemcpyHostToDevice);
     return e;
 }
 
@@ -751,6 +779,7 @@ Dev make_dev(const DevBufs& b, const uint8_t* prg, const uint8_t* chr, const uin
     d.n = b.n; d.n_pad = b.n_pad; d.slab = b.slab; d.vram = b.vram; d.scal = b.scal; d.logs = b.logs;
     d.log_cap = b.log_cap; d.prg = prg; d.chr = chr;
     d.uop = reinterpret_cast<const uint32_t*>(prg + PRG_UOP_OFF);
+    d.dop = reinterpret_cast<const uint32_t*>(prg + PRG_DOP_OFF);
     for (int i = 0; i < 4; i++) d.nt[i] = nt[i];
     d.lut = lut; d.err = err;
     return d;

@@ -19,6 +19,7 @@ struct Hot {
     uint32_t zero_skip, bad;
     uint32_t ux, uy;  // micro-op of the instruction at pc (fme_defs.h); zero outside PRG
     uint32_t icount;  // instructions executed since hot_init (emulated-work counter)
+    uint32_t rf;      // A | X<<8 | Y<<16 | SP<<24 while the datapath (fme_dp.h) owns the registers
 };
 
 // Exact slow paths (the Core methods), out of line so the hot loop stays small.

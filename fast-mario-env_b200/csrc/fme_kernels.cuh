@@ -15,6 +15,7 @@ extern uint32_t g_host_dtab[256];
 #include "fme_core.h"
 #include "fme_agent.h"
 #include "fme_fast.h"
+#include "fme_dp.h"
 #include "fme_render.h"
 
 namespace fme {
@@ -33,6 +34,7 @@ struct Dev {
     int log_cap;
     const uint8_t* prg;
     const uint32_t* uop; // per-PC micro-ops (fme_tables.h build_uops), stored right after the 32 KB PRG
+    const uint32_t* dop; // per-PC datapath micro-ops (fme_dp.h, build_dops), after the micro-ops
     const uint8_t* chr;
     uint32_t nt[4];
     const uint8_t* lut; // 256 gray LUT (global)

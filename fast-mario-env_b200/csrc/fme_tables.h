@@ -7,6 +7,7 @@
 #include <vector>
 #include "fme_defs.h"
 #include "fme_render.h"
+#include "fme_dp.h"
 
 namespace fme {
 namespace tables {
@@ -241,6 +242,15 @@ inline void build_uops(const uint8_t* prg, const uint32_t* dtab, uint32_t* out /
         }
         out[2 * (a - 0x8000u)] = hid | (opc << 8) | (op << 16) | (pen << 21) | (len << 22) | ((idle ? 1u : 0u) << 24);
         out[2 * (a - 0x8000u) + 1] = (w & 0xffffu) | (cyc << 16) | (extra << 24);
+    }
+}
+
+// Datapath micro-ops (fme_dp.h) of every PRG address, from the exact micro-op table (2 x 32768 words each).
+inline void build_dops(const uint32_t* uops, uint32_t* out) {
+    for (uint32_t i = 0; i < 0x8000u; i++) {
+        const uint2 d = make_dop(uops[2 * i], uops[2 * i + 1]);
+        out[2 * i] = d.x;
+        out[2 * i + 1] = d.y;
     }
 }
 

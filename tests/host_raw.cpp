@@ -1,8 +1,9 @@
 // Host build of the engine's emulation headers, used by the CPU test suite (tests/test_host_engine.py).
 //
 // Raw consoles are stepped one NES frame at a time with the code the GPU kernels run: Core (fme_core.h), the
-// register-resident fast path and its per-PC micro-ops (fme_fast.h, fme_tables.h) and the frame bookkeeping
-// of fme_agent.h. Each console has a whole group slab to itself and uses lane 0 of it, so memory is laid out
+// register-resident fast path and its per-PC micro-ops (fme_fast.h, fme_tables.h), the data-driven datapath
+// and its micro-ops (fme_dp.h, lane_step: the per-lane meaning of the step kernel's two-phase warp loop) and
+// the frame bookkeeping of fme_agent.h. Each console has a whole group slab to itself and uses lane 0 of it, so memory is laid out
 // exactly as in the kernels. The per-frame flow follows k_raw: scalars in, begin_frame, hot_step until the
 // frame end, end_frame / close_frame, scalars out. No pixels are drawn (the GPU renderer is warp code); the
 // PPU log is produced and discarded, so its catch-up and logging paths still run.
@@ -14,6 +15,7 @@
 #include "fme_agent.h"
 #include "fme_tables.h"
 #include "fme_fast.h"
+#include "fme_dp.h"
 
 namespace fme { uint32_t g_host_dtab[256]; }
 using namespace fme;
@@ -31,6 +33,7 @@ struct HostRaw {
     std::vector<uint8_t> vram;     // n x VRAM_BYTES
     std::vector<uint32_t> words;   // n x S_WORDS
     std::vector<uint8_t> log;      // one log slot, reused by every console and frame
+    std::vector<uint32_t> dops;    // datapath micro-ops (2 words per PRG address)
 };
 
 void bind(HostRaw* r, Core& c, int e) {
@@ -67,6 +70,8 @@ void* hr_create(const uint8_t* rom, int64_t len, int n) {
     else { r->nt[2] = r->nt[3] = 0x400; }               // horizontal mirroring
     tables::build_dtab(g_host_dtab);
     tables::build_uops(r->prg.data(), g_host_dtab, reinterpret_cast<uint32_t*>(r->prg.data() + 0x8000));
+    r->dops.assign((size_t)UOP_WORDS, 0);
+    tables::build_dops(reinterpret_cast<const uint32_t*>(r->prg.data() + 0x8000), r->dops.data());
     r->slab.assign((size_t)n * SLAB_BYTES, 0);
     r->vram.assign((size_t)n * VRAM_BYTES, 0);
     r->words.assign((size_t)n * S_WORDS, 0);
@@ -97,8 +102,11 @@ void hr_frame(void* h, const uint8_t* buttons) {
         const Fast fst{c.ram, r->prg.data(), reinterpret_cast<const uint32_t*>(r->prg.data() + 0x8000)};
         Hot hot{};
         hot_in(hot, c, fst);
-        while (hot_step(hot, c, fst)) {
+        rf_pack(hot);
+        dfetch(hot, r->dops.data());
+        while (lane_step(hot, c, fst, r->dops.data())) {
         }
+        rf_unpack(hot);
         hot_out(hot, c);
         c.end_frame();
         close_frame(c, slot);

@@ -194,7 +194,7 @@ def reference_cuda(rom, E, steps, warmup, dev):
     g = torch.Generator(device=dev)
     g.manual_seed(4321)
     acts = torch.randint(0, 7, (warmup + steps, E), dtype=torch.int64, device=dev, generator=g)
-    out = {"config": "config1 with maxpool=False", "n_envs": E, "steps": steps}
+    out = {"config": "the workload above with maxpool=False", "n_envs": E, "steps": steps}
     with tempfile.NamedTemporaryFile(suffix=".nes", delete=False) as f:
         f.write(rom)
         rom_path = f.name
@@ -481,7 +481,7 @@ def main():
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cb = cpu_baseline(rom, args)
     ref_cuda = None
-    if rank == 0 and world == 1 and not args.no_ref_gpu and not args.divergent:
+    if rank == 0 and world == 1 and not args.no_ref_gpu:
         ref_cuda = reference_cuda(rom, E, args.steps, args.warmup, dev)
     if rank == 0:
         line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,

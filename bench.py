@@ -247,6 +247,7 @@ def run_ppo(args, rank, world, dev, dist):
     torch.cuda.synchronize(dev)
     if dist:
         dist.barrier()
+    clocks = ClockSampler(torch.cuda.current_device())
     e0, e1, em = (torch.cuda.Event(enable_timing=True) for _ in range(3))
     coll = 0.0
     e0.record()
@@ -258,6 +259,7 @@ def run_ppo(args, rank, world, dev, dist):
         coll += c0.elapsed_time(c1)
     e1.record()
     torch.cuda.synchronize(dev)
+    clk = clocks.stop()
     if bool(tr.trunc_overflow):
         raise RuntimeError("time-limit truncations exceeded PPOConfig.trunc_budget in a rollout step")
     ms = e0.elapsed_time(e1)
@@ -266,7 +268,8 @@ def run_ppo(args, rank, world, dev, dist):
     if rank == 0:
         print(json.dumps({"metric": "PPO samples/sec (config 4)", "value": samples / (ms_max / 1000.0), "unit": "samples/s",
                           "n_gpus": world, "iterations": iters, "ms_per_iteration": ms_max / iters,
-                          "rollout_ms_per_iteration": coll / iters, "higher_is_better": True, "scaling": "weak",
+                          "rollout_ms_per_iteration": coll / iters, "clocks": clk, "higher_is_better": True,
+                          "scaling": "weak",
                           "dtype": "fp32", "data": "synthetic",
                           "config": {"workload": "config4: Nature-CNN PPO on config-1 envs", "n_envs_per_gpu": E,
                                      "n_steps": 128, "epochs": 4, "minibatch": 1024, "gamma": 0.99, "lam": 0.95,

@@ -16,7 +16,7 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 CSRC = os.path.join(HERE, "csrc")
 LIB = os.path.join(HERE, "libfme_cuda.so")
 SOURCES = ["fme.cu"]
-DEPS = ["fme.cu", "fme_kernels.cuh", "fme_core.h", "fme_agent.h", "fme_render.h", "fme_defs.h", "fme_tables.h", "fme_fast.h", "fme_ppo.cuh", "fme_replay.cuh"]
+DEPS = ["fme.cu", "fme_kernels.cuh", "fme_core.h", "fme_agent.h", "fme_render.h", "fme_defs.h", "fme_tables.h", "fme_fast.h", "fme_dp.h", "fme_ppo.cuh", "fme_replay.cuh"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 

@@ -75,7 +75,7 @@ __global__ void __launch_bounds__(32) k_boot(BootParams P) {
     // Boot protocol of SuperMarioBrosEnv (fastmario.cpp:422-445), one frame per call of the state machine:
     // phase 0 fa(8), 1 fa(0), then loop A {2: fa(8); write level; 3: fa(0); $7A0=0} while time==0,
     // then loop B {4: fa(8), 5: fa(0)} while time >= tl.
-    const Fast fst{c.ram, d.prg, d.uop};
+    const Fast fst{c.ram, c.ramh, d.prg, d.uop};
     Hot h;
     h.icount = 0;
     hot_in(h, c, fst);
@@ -164,7 +164,8 @@ __global__ void __launch_bounds__(32, 1) k_step(StepParams P) {
 
     Core c;
     bind_core(c, d, sm, lane, e);
-    c.oam = gslab + SLAB_OAM_OFF + lane * 4;   // OAM and palette stay in HBM (L1-cached)
+    c.ramh = gslab + SLAB_RAM_OFF + lane * 4;  // RAM from RAM_SMEM_END up, OAM and palette stay in HBM (L1-cached)
+    c.oam = gslab + SLAB_OAM_OFF + lane * 4;
     c.pal = gslab + SLAB_PAL_OFF + lane * 4;
     uint32_t w[S_WORDS];
     for (int k = 0; k < S_WORDS; k++) w[k] = 0;
@@ -190,7 +191,7 @@ __global__ void __launch_bounds__(32, 1) k_step(StepParams P) {
     // minimum key and those lanes take one step on the exact path (I/O, PPU catch-up and NMI, the idle-loop
     // fast-forward, the frame end), all lanes at that PC together. Lanes are independent, so the order in
     // which the warp serves them changes no result.
-    const Fast fst{c.ram, d.prg, d.uop};
+    const Fast fst{c.ram, c.ramh, d.prg, d.uop};
     const uint32_t ip0 = __ldg(d.uop + UOP_WORDS), ip1 = __ldg(d.uop + UOP_WORDS + 1);
     Hot h;
     h.icount = 0;
@@ -479,7 +480,7 @@ __global__ void __launch_bounds__(32) k_reset(StepParams P) {
         load_words(d, e, w);
         Core c;
         uint8_t* slab = d.slab + (size_t)g * SLAB_BYTES;   // the lane-interleaved slab itself, in HBM
-        c.ram = slab + SLAB_RAM_OFF + lane * 4; c.oam = slab + SLAB_OAM_OFF + lane * 4;
+        c.ram = slab + SLAB_RAM_OFF + lane * 4; c.ramh = c.ram; c.oam = slab + SLAB_OAM_OFF + lane * 4;
         c.pal = slab + SLAB_PAL_OFF + lane * 4; c.vram = d.vram + (size_t)e * VRAM_BYTES;
         c.load_scalars(w);
         c.bad_ops = w[S_BADOPS]; c.status = w[S_STATUS];
@@ -527,7 +528,7 @@ __global__ void __launch_bounds__(32) k_raw(RawParams P) {
     uint8_t* slot = d.logs + slot_off(e, 0, d.log_cap);
     bool running = active;
     if (active) begin_frame(c, slot, P.buttons[e], d.log_cap);
-    const Fast fst{c.ram, d.prg, d.uop};
+    const Fast fst{c.ram, c.ramh, d.prg, d.uop};
     Hot h;
     h.icount = 0;
     hot_in(h, c, fst);
@@ -702,6 +703,10 @@ int ensure_constants(int device) {
     CK(cudaFuncSetAttribute(k_resize, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
     CK(cudaFuncSetAttribute(k_power, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
     CK(cudaFuncSetAttribute(k_render, cudaFuncAttributeMaxDynamicSharedMemorySize, RB_BYTES));
+#ifdef FME_STEP_CARVEOUT
+    CK(cudaFuncSetAttribute(k_step<true>, cudaFuncAttributePreferredSharedMemoryCarveout, FME_STEP_CARVEOUT));
+    CK(cudaFuncSetAttribute(k_render, cudaFuncAttributePreferredSharedMemoryCarveout, FME_STEP_CARVEOUT));
+#endif
     g_const_ctx[device] = ctx;
     return FME_OK;
 }

@@ -132,7 +132,7 @@ FME_HD void materialise_state(Core& c) {
 // ---------------------------------------------------------------- console image <-> lane state
 FME_HD void image_to_lane(const uint8_t* img, Core& c, uint32_t* scal_words) {
     for (int w = 0; w < RAM_BYTES / 4; w++)
-        *reinterpret_cast<uint32_t*>(c.ram + (w << 7)) = reinterpret_cast<const uint32_t*>(img + IMG_RAM)[w];
+        *reinterpret_cast<uint32_t*>(c.ram_at((uint32_t)w * 4)) = reinterpret_cast<const uint32_t*>(img + IMG_RAM)[w];
     for (int w = 0; w < OAM_BYTES / 4; w++)
         *reinterpret_cast<uint32_t*>(c.oam + (w << 7)) = reinterpret_cast<const uint32_t*>(img + IMG_OAM)[w];
     for (int w = 0; w < PAL_BYTES / 4; w++)
@@ -145,7 +145,7 @@ FME_HD void image_to_lane(const uint8_t* img, Core& c, uint32_t* scal_words) {
 }
 FME_HD void lane_to_image(const Core& c, uint8_t* img) {
     for (int w = 0; w < RAM_BYTES / 4; w++)
-        reinterpret_cast<uint32_t*>(img + IMG_RAM)[w] = *reinterpret_cast<const uint32_t*>(c.ram + (w << 7));
+        reinterpret_cast<uint32_t*>(img + IMG_RAM)[w] = *reinterpret_cast<const uint32_t*>(c.ram_at((uint32_t)w * 4));
     for (int w = 0; w < OAM_BYTES / 4; w++)
         reinterpret_cast<uint32_t*>(img + IMG_OAM)[w] = *reinterpret_cast<const uint32_t*>(c.oam + (w << 7));
     for (int w = 0; w < PAL_BYTES / 4; w++)

@@ -61,6 +61,7 @@ struct Core {
     uint32_t ev_y;                   // scanline of that evaluation
     // ---- memory
     uint8_t* ram;   // lane base of the RAM slab (shared memory on the device)
+    uint8_t* ramh;  // lane base for addresses >= RAM_SMEM_END (== ram when the whole RAM is in one place)
     uint8_t* oam;
     uint8_t* pal;
     uint8_t* vram;  // this env's 2 KB VRAM (global)
@@ -79,8 +80,12 @@ struct Core {
     uint32_t status;
 
     // ================================================================ memory helpers
-    FME_HD uint32_t RAM(uint32_t a) const { return ram[il(a & 0x7ffu)]; }
-    FME_HD void RAMW(uint32_t a, uint32_t v_) { ram[il(a & 0x7ffu)] = (uint8_t)v_; }
+    FME_HD uint8_t* ram_at(uint32_t a) const {
+        const uint32_t m = a & 0x7ffu;
+        return (m < RAM_SMEM_END ? ram : ramh) + il(m);
+    }
+    FME_HD uint32_t RAM(uint32_t a) const { return *ram_at(a); }
+    FME_HD void RAMW(uint32_t a, uint32_t v_) { *ram_at(a) = (uint8_t)v_; }
     FME_HD uint32_t OAM(uint32_t i) const { return oam[il(i & 0xffu)]; }
     FME_HD void OAMW(uint32_t i, uint32_t v_) { oam[il(i & 0xffu)] = (uint8_t)v_; }
     FME_HD uint32_t PAL(uint32_t i) const { return pal[il(i & 0x1fu)]; }

@@ -31,6 +31,16 @@ constexpr int SLAB_OAM_OFF = RAM_BYTES * LANES;                  // 65536
 constexpr int SLAB_PAL_OFF = SLAB_OAM_OFF + OAM_BYTES * LANES;   // 73728
 constexpr int SLAB_BYTES = SLAB_PAL_OFF + PAL_BYTES * LANES;     // 74752
 
+// k_step's emulation keeps RAM addresses below RAM_SMEM_END in shared memory and reaches the rest in the
+// HBM slab itself (same lane-interleaved layout, through L1). Both halves are addressed through Core::RAM
+// and Fast::R/W, which pick the base by address; at 0x800 the whole RAM is in shared memory.
+#ifndef FME_RAM_SMEM_END
+#define FME_RAM_SMEM_END 0x800
+#endif
+constexpr uint32_t RAM_SMEM_END = FME_RAM_SMEM_END;
+static_assert(RAM_SMEM_END % 4 == 0 && RAM_SMEM_END >= 0x200 && RAM_SMEM_END <= (uint32_t)RAM_BYTES,
+              "the split is word aligned and keeps zero page and stack in shared memory");
+
 constexpr int FRAME_ITERS = 29781;           // CPU iterations per emulated frame (nes_core.hpp:53)
 constexpr int FRAME_CALLS = 3 * FRAME_ITERS;  // PPU calls per emulated frame
 constexpr int OBS = 84;

@@ -70,6 +70,7 @@ __device__ __forceinline__ size_t slot_off(int e, int s, int cap) {
 // ---------------------------------------------------------------- per-lane console binding
 __device__ __forceinline__ void bind_core(Core& c, const Dev& d, uint8_t* sm, int lane, int e) {
     c.ram = sm + SLAB_RAM_OFF + lane * 4;
+    c.ramh = c.ram;
     c.oam = sm + SLAB_OAM_OFF + lane * 4;
     c.pal = sm + SLAB_PAL_OFF + lane * 4;
     c.vram = d.vram + (size_t)e * VRAM_BYTES;
@@ -113,10 +114,9 @@ __device__ __forceinline__ void copy_slab(uint8_t* dst, const uint8_t* src, int 
 #pragma unroll 4
     for (int i = lane; i < nbytes / 16; i += 32) d[i] = s[i];
 }
-// k_step keeps only the group's RAM in shared memory (OAM and palette are used by the rarer PPU paths and
-// stay in the HBM slab, reached through L1): 64 KB per CTA leaves room for a render CTA next to three
-// emulation CTAs on an SM.
-constexpr int STEP_SMEM = SLAB_OAM_OFF;
+// k_step keeps only the group's RAM below RAM_SMEM_END in shared memory (OAM, palette and the RAM above it
+// stay in the HBM slab, reached through L1).
+constexpr int STEP_SMEM = (int)RAM_SMEM_END * LANES;
 
 // ---------------------------------------------------------------- warp renderer
 // Shared-memory layout of the render phase (reuses the emulation slab region).

@@ -2,8 +2,9 @@
 //
 // The timed step (fme_step) is two kernels per env slice (up to four slices, each forked from the caller's
 // stream onto a high-priority emulation stream and a low-priority render stream, joined back with events):
-//   k_step<true>   emulation, one CTA = one warp = 32 envs: the group's 64 KB of RAM in shared memory (OAM and
-//                  palette read through L1 from the HBM slab), `skip` frames (+ busy-state frames) per env with
+//   k_step<true>   emulation, one CTA = one warp = 32 envs: the group's RAM below a boundary in shared memory
+//                  (48 KB, or 23 KB for large env counts; the rest of RAM, OAM and palette read through L1
+//                  from the HBM slab), `skip` frames (+ busy-state frames) per env with
 //                  per-frame PPU logs, rewards / dones / infos, auto-reset from the reset cache, and a render job
 //                  word per env.
 //   k_render       one warp per (env, band of 60 screen rows): the frame-stack shift of the band, replay of the
@@ -75,7 +76,7 @@ __global__ void __launch_bounds__(32) k_boot(BootParams P) {
     // Boot protocol of SuperMarioBrosEnv (fastmario.cpp:422-445), one frame per call of the state machine:
     // phase 0 fa(8), 1 fa(0), then loop A {2: fa(8); write level; 3: fa(0); $7A0=0} while time==0,
     // then loop B {4: fa(8), 5: fa(0)} while time >= tl.
-    const Fast fst{c.ram, c.ramh, d.prg, d.uop};
+    const Fast fst{c.ram, c.ramh, c.ram_end, d.prg, d.uop};
     Hot h;
     h.icount = 0;
     hot_in(h, c, fst);
@@ -159,12 +160,14 @@ __global__ void __launch_bounds__(32, 1) k_step(StepParams P) {
     const int cap = d.log_cap;
     const AgentCfg cfg = agent_cfg(P);
     uint8_t* const gslab = d.slab + (size_t)g * SLAB_BYTES;
-    copy_slab(sm, gslab, lane, STEP_SMEM);
+    const int ram_sm = (int)P.ram_end * LANES;   // bytes of the slab's RAM held in shared memory
+    copy_slab(sm, gslab, lane, ram_sm);
     __syncwarp();
 
     Core c;
     bind_core(c, d, sm, lane, e);
-    c.ramh = gslab + SLAB_RAM_OFF + lane * 4;  // RAM from RAM_SMEM_END up, OAM and palette stay in HBM (L1-cached)
+    c.ramh = gslab + SLAB_RAM_OFF + lane * 4;  // RAM from ram_end up, OAM and palette stay in HBM (L1-cached)
+    c.ram_end = P.ram_end;
     c.oam = gslab + SLAB_OAM_OFF + lane * 4;
     c.pal = gslab + SLAB_PAL_OFF + lane * 4;
     uint32_t w[S_WORDS];
@@ -191,7 +194,7 @@ __global__ void __launch_bounds__(32, 1) k_step(StepParams P) {
     // minimum key and those lanes take one step on the exact path (I/O, PPU catch-up and NMI, the idle-loop
     // fast-forward, the frame end), all lanes at that PC together. Lanes are independent, so the order in
     // which the warp serves them changes no result.
-    const Fast fst{c.ram, c.ramh, d.prg, d.uop};
+    const Fast fst{c.ram, c.ramh, c.ram_end, d.prg, d.uop};
     const uint32_t ip0 = __ldg(d.uop + UOP_WORDS), ip1 = __ldg(d.uop + UOP_WORDS + 1);
     Hot h;
     h.icount = 0;
@@ -287,7 +290,7 @@ __global__ void __launch_bounds__(32, 1) k_step(StepParams P) {
         if (c.status) atomicOr(d.err, c.status);
     }
     __syncwarp();
-    copy_slab(gslab, sm, lane, STEP_SMEM);
+    copy_slab(gslab, sm, lane, ram_sm);
     __syncwarp();
 
     const uint32_t summary = (active ? 1u : 0u) | (pooled ? 2u : 0u) | ((uint32_t)cur_slot << 2) | (ended ? 8u : 0u);
@@ -480,7 +483,7 @@ __global__ void __launch_bounds__(32) k_reset(StepParams P) {
         load_words(d, e, w);
         Core c;
         uint8_t* slab = d.slab + (size_t)g * SLAB_BYTES;   // the lane-interleaved slab itself, in HBM
-        c.ram = slab + SLAB_RAM_OFF + lane * 4; c.ramh = c.ram; c.oam = slab + SLAB_OAM_OFF + lane * 4;
+        c.ram = slab + SLAB_RAM_OFF + lane * 4; c.ramh = c.ram; c.ram_end = RAM_BYTES; c.oam = slab + SLAB_OAM_OFF + lane * 4;
         c.pal = slab + SLAB_PAL_OFF + lane * 4; c.vram = d.vram + (size_t)e * VRAM_BYTES;
         c.load_scalars(w);
         c.bad_ops = w[S_BADOPS]; c.status = w[S_STATUS];
@@ -528,7 +531,7 @@ __global__ void __launch_bounds__(32) k_raw(RawParams P) {
     uint8_t* slot = d.logs + slot_off(e, 0, d.log_cap);
     bool running = active;
     if (active) begin_frame(c, slot, P.buttons[e], d.log_cap);
-    const Fast fst{c.ram, c.ramh, d.prg, d.uop};
+    const Fast fst{c.ram, c.ramh, c.ram_end, d.prg, d.uop};
     Hot h;
     h.icount = 0;
     hot_in(h, c, fst);
@@ -703,10 +706,6 @@ int ensure_constants(int device) {
     CK(cudaFuncSetAttribute(k_resize, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
     CK(cudaFuncSetAttribute(k_power, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
     CK(cudaFuncSetAttribute(k_render, cudaFuncAttributeMaxDynamicSharedMemorySize, RB_BYTES));
-#ifdef FME_STEP_CARVEOUT
-    CK(cudaFuncSetAttribute(k_step<true>, cudaFuncAttributePreferredSharedMemoryCarveout, FME_STEP_CARVEOUT));
-    CK(cudaFuncSetAttribute(k_render, cudaFuncAttributePreferredSharedMemoryCarveout, FME_STEP_CARVEOUT));
-#endif
     g_const_ctx[device] = ctx;
     return FME_OK;
 }
@@ -890,6 +889,7 @@ struct FmeEnv {
     // followed by its render launch on a low-priority stream: the renders of finished slices fill the SMs
     // that the slower slices' last warps leave idle. Fork/join with events on the caller's stream.
     int nch = 0;
+    uint32_t ram_end = RAM_END_DEEP;   // k_step's shared-memory RAM boundary for this env count (step_ram_end)
     cudaStream_t s_emu[kChunks] = {}, s_rnd[kChunks] = {};
     cudaEvent_t ev_in = nullptr, ev_emu[kChunks] = {}, ev_rnd[kChunks] = {};
     // fme_step_to_host: early copy of the old frames (s_copy, one event per slice) and the host-side fix-up
@@ -948,6 +948,14 @@ static void free_env(FmeEnv* v) {
     delete v;
 }
 
+// k_step's RAM boundary for a step of `groups` CTAs on `sms` SMs. While the deep layout (4 CTAs per SM)
+// runs them in a few waves, the step is set by its slowest warps and the per-instruction latency of the
+// shared-memory RAM wins; past about 4.5 waves it is throughput-bound and the wide layout's 8 CTAs per SM
+// win (on a B200: deep ahead up to 65,536 envs, wide ahead from 98,304 envs, by 14 % at 262,144).
+static uint32_t step_ram_end(int groups, int sms) {
+    return (double)groups > 4.5 * 4.0 * (double)(sms > 0 ? sms : 1) ? RAM_END_WIDE : RAM_END_DEEP;
+}
+
 static StepParams base_params(FmeEnv* v, const Dev& d) {
     StepParams P;
     memset(&P, 0, sizeof(P));
@@ -963,6 +971,7 @@ static StepParams base_params(FmeEnv* v, const Dev& d) {
     P.cache.img = v->d_cache_img; P.cache.obs = v->d_cache_obs; P.cache.meta = v->d_cache_meta;
     P.n_levels = v->nl;
     P.level_img = v->d_level_img; P.level_obs0 = v->d_obs0; P.level_meta = v->d_level_meta;
+    P.ram_end = RAM_BYTES;   // the reset-cache builder holds the whole slab in shared memory
     return P;
 }
 
@@ -1012,6 +1021,9 @@ static int create_impl(const FmeConfig* cfg, const uint8_t* rom, int64_t rom_len
         CK(cudaDeviceGetStreamPriorityRange(&lo, &hi));
         const int groups = (C.n_envs + 31) / 32;
         v->nch = groups < kChunks ? groups : kChunks;
+        int sms = 0;
+        CK(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, C.device));
+        v->ram_end = step_ram_end(groups, sms);
         CK(cudaEventCreateWithFlags(&v->ev_in, cudaEventDisableTiming));
         CK(cudaStreamCreateWithPriority(&v->s_copy, cudaStreamNonBlocking, lo));
         CK(cudaEventCreateWithFlags(&v->ev_copy, cudaEventDisableTiming));
@@ -1264,7 +1276,8 @@ static int launch_step_impl(FmeEnv* v, const int64_t* d_actions, void* stream, b
             const int e0 = g0 * 32, e1 = g1 * 32 < v->n ? g1 * 32 : v->n;
             CK(cudaStreamWaitEvent(v->s_emu[c], v->ev_in, 0));
             P.group_base = g0;
-            k_step<true><<<g1 - g0, 32, STEP_SMEM, v->s_emu[c]>>>(P);
+            P.ram_end = v->ram_end;
+            k_step<true><<<g1 - g0, 32, (size_t)v->ram_end * LANES, v->s_emu[c]>>>(P);
             CK(cudaEventRecord(v->ev_emu[c], v->s_emu[c]));
             CK(cudaStreamWaitEvent(v->s_rnd[c], v->ev_emu[c], 0));
             // the device copy of the old frames must read them before the render moves them

@@ -61,7 +61,8 @@ struct Core {
     uint32_t ev_y;                   // scanline of that evaluation
     // ---- memory
     uint8_t* ram;   // lane base of the RAM slab (shared memory on the device)
-    uint8_t* ramh;  // lane base for addresses >= RAM_SMEM_END (== ram when the whole RAM is in one place)
+    uint8_t* ramh;  // lane base for addresses >= ram_end (== ram when the whole RAM is in one place)
+    uint32_t ram_end;
     uint8_t* oam;
     uint8_t* pal;
     uint8_t* vram;  // this env's 2 KB VRAM (global)
@@ -82,7 +83,7 @@ struct Core {
     // ================================================================ memory helpers
     FME_HD uint8_t* ram_at(uint32_t a) const {
         const uint32_t m = a & 0x7ffu;
-        return (m < RAM_SMEM_END ? ram : ramh) + il(m);
+        return (m < ram_end ? ram : ramh) + il(m);
     }
     FME_HD uint32_t RAM(uint32_t a) const { return *ram_at(a); }
     FME_HD void RAMW(uint32_t a, uint32_t v_) { *ram_at(a) = (uint8_t)v_; }

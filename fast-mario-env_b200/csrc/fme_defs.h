@@ -31,15 +31,17 @@ constexpr int SLAB_OAM_OFF = RAM_BYTES * LANES;                  // 65536
 constexpr int SLAB_PAL_OFF = SLAB_OAM_OFF + OAM_BYTES * LANES;   // 73728
 constexpr int SLAB_BYTES = SLAB_PAL_OFF + PAL_BYTES * LANES;     // 74752
 
-// k_step's emulation keeps RAM addresses below RAM_SMEM_END in shared memory and reaches the rest in the
-// HBM slab itself (same lane-interleaved layout, through L1). Both halves are addressed through Core::RAM
-// and Fast::R/W, which pick the base by address; at 0x800 the whole RAM is in shared memory.
-#ifndef FME_RAM_SMEM_END
-#define FME_RAM_SMEM_END 0x800
-#endif
-constexpr uint32_t RAM_SMEM_END = FME_RAM_SMEM_END;
-static_assert(RAM_SMEM_END % 4 == 0 && RAM_SMEM_END >= 0x200 && RAM_SMEM_END <= (uint32_t)RAM_BYTES,
-              "the split is word aligned and keeps zero page and stack in shared memory");
+// k_step's emulation keeps the RAM addresses below a boundary (ram_end) in shared memory and reaches the rest
+// in the HBM slab itself (same lane-interleaved layout, through L1). Both parts are addressed through
+// Core::RAM and Fast::R/W, which pick the base by address; the other kernels hold the whole RAM in shared
+// memory (ram_end = 0x800). The step picks the boundary by how many CTAs it runs: latency first while they
+// fill the SMs in a few waves, residency first beyond that.
+//  * RAM_END_DEEP: 48 KB per CTA of 32 envs, so four fit an SM's 196 KB shared-memory configuration (three at
+//    64 KB), leaving 60 KB of L1 for each env's top 512 bytes of RAM, OAM and palette;
+//  * RAM_END_WIDE: 23 KB per CTA, eight per SM in the same configuration.
+constexpr uint32_t RAM_END_DEEP = 0x600, RAM_END_WIDE = 0x2e0;
+static_assert(RAM_END_DEEP % 4 == 0 && RAM_END_WIDE % 4 == 0 && RAM_END_WIDE >= 0x200 &&
+              RAM_END_DEEP <= (uint32_t)RAM_BYTES, "boundaries are word aligned and keep zero page and stack in shared memory");
 
 constexpr int FRAME_ITERS = 29781;           // CPU iterations per emulated frame (nes_core.hpp:53)
 constexpr int FRAME_CALLS = 3 * FRAME_ITERS;  // PPU calls per emulated frame

@@ -246,7 +246,7 @@ FME_HD bool dp_exec(Hot& h, const Fast& f, const uint32_t* dops, bool run = true
     const uint32_t zb = (W + ((dx & D_INX) ? X : 0u)) & 0xffu;
     const uint32_t a0 = pull ? (0x100u | ((SP + 1u) & 0xffu)) : zb;
     const uint32_t a1 = pull ? (0x100u | ((SP + 2u) & 0xffu)) : ((zb + 1u) & 0xffu);
-    const uint32_t p0 = f.R(a0), p1 = f.R(a1);
+    const uint32_t p0 = f.Rz(a0), p1 = f.Rz(a1);
     const uint32_t ptr = p0 | (p1 << 8);
     // next pc, and its dop loaded right away (branches test the flags before this instruction)
     const uint32_t pcm = (dy >> 27) & 3u;
@@ -293,8 +293,8 @@ FME_HD bool dp_exec(Hot& h, const Fast& f, const uint32_t* dops, bool run = true
     const bool jsr = (dy & D_JSR) != 0u;
     if (ok && dst == DS_MEM && ea < 0x2000u) f.W(ea, r);
     const uint32_t ret = (npc + 1u) & 0xffffu;
-    if (ok && jsr) f.W(0x100u | SP, ret >> 8);
-    if (ok && jsr) f.W(0x100u | ((SP - 1u) & 0xffu), ret & 0xffu);
+    if (ok && jsr) f.Wz(0x100u | SP, ret >> 8);
+    if (ok && jsr) f.Wz(0x100u | ((SP - 1u) & 0xffu), ret & 0xffu);
     // registers: the destination byte of the register file, then the stack pointer change in its top byte
     const uint32_t sh = 8u * ((dst - DS_A) & 3u);
     const uint32_t nrf = (dst >= DS_A && dst <= DS_SP) ? ((rf & ~(0xffu << sh)) | (r << sh)) : rf;

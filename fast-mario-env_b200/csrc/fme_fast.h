@@ -35,17 +35,21 @@ FME_NI int32_t slow_execute(Core& c, int32_t J, uint32_t opc) {
 
 struct Fast {
     uint8_t* ram;            // lane base of the RAM slab
-    uint8_t* ramh;           // lane base for addresses >= RAM_SMEM_END
+    uint8_t* ramh;           // lane base for addresses >= ram_end
+    uint32_t ram_end;
     const uint8_t* prg;
     const uint32_t* uop;     // per-PC micro-ops, 2 words per address $8000-$FFFF
 
     FME_HD uint32_t P(uint32_t a) const { return FME_LDG(prg + (a & 0x7fffu)); }
     FME_HD uint8_t* at(uint32_t a) const {
         const uint32_t m = a & 0x7ffu;
-        return (m < RAM_SMEM_END ? ram : ramh) + il(m);
+        return (m < ram_end ? ram : ramh) + il(m);
     }
     FME_HD uint32_t R(uint32_t a) const { return *at(a); }
     FME_HD void W(uint32_t a, uint32_t v) const { *at(a) = (uint8_t)v; }
+    // zero page and stack ($0000-$01FF, below every boundary): no base select
+    FME_HD uint32_t Rz(uint32_t a) const { return ram[il(a & 0x1ffu)]; }
+    FME_HD void Wz(uint32_t a, uint32_t v) const { ram[il(a & 0x1ffu)] = (uint8_t)v; }
     // side-effect-free read of an address outside $2000-$7FFF
     FME_HD uint32_t M(uint32_t a) const { return a >= 0x8000u ? P(a) : R(a); }
     FME_HD static bool io(uint32_t a) { return a >= 0x2000u && a < 0x8000u; }

@@ -58,6 +58,7 @@ struct StepParams {
     // MODE_STEP with k_render: per-env render job word (bit 0 active, 1 pooled, 2 slot, 3 episode ended)
     uint32_t* jobs;
     int group_base;  // first group of this launch (k_step block b handles group group_base + b)
+    uint32_t ram_end;   // RAM below this address in shared memory (RAM_END_DEEP / RAM_END_WIDE; 0x800 for MODE_NOOP)
     // MODE_NOOP: where to write the cache entry for this noop step
     uint8_t* out_img; uint8_t* out_obs; int32_t* out_meta; int noop_j;
     const uint8_t* level_img; const uint8_t* level_obs0; const int32_t* level_meta;  // backups (x0, t0)
@@ -71,6 +72,7 @@ __device__ __forceinline__ size_t slot_off(int e, int s, int cap) {
 __device__ __forceinline__ void bind_core(Core& c, const Dev& d, uint8_t* sm, int lane, int e) {
     c.ram = sm + SLAB_RAM_OFF + lane * 4;
     c.ramh = c.ram;
+    c.ram_end = RAM_BYTES;
     c.oam = sm + SLAB_OAM_OFF + lane * 4;
     c.pal = sm + SLAB_PAL_OFF + lane * 4;
     c.vram = d.vram + (size_t)e * VRAM_BYTES;
@@ -114,9 +116,9 @@ __device__ __forceinline__ void copy_slab(uint8_t* dst, const uint8_t* src, int 
 #pragma unroll 4
     for (int i = lane; i < nbytes / 16; i += 32) d[i] = s[i];
 }
-// k_step keeps only the group's RAM below RAM_SMEM_END in shared memory (OAM, palette and the RAM above it
-// stay in the HBM slab, reached through L1).
-constexpr int STEP_SMEM = (int)RAM_SMEM_END * LANES;
+// k_step keeps only the group's RAM below StepParams::ram_end in shared memory (OAM, palette and the RAM above
+// it stay in the HBM slab, reached through L1); this many bytes at most.
+constexpr int STEP_SMEM = (int)RAM_END_DEEP * LANES;
 
 // ---------------------------------------------------------------- warp renderer
 // Shared-memory layout of the render phase (reuses the emulation slab region).

@@ -40,6 +40,7 @@ void bind(HostRaw* r, Core& c, int e) {
     uint8_t* s = r->slab.data() + (size_t)e * SLAB_BYTES;
     c.ram = s + SLAB_RAM_OFF;
     c.ramh = c.ram;
+    c.ram_end = RAM_BYTES;
     c.oam = s + SLAB_OAM_OFF;
     c.pal = s + SLAB_PAL_OFF;
     c.vram = r->vram.data() + (size_t)e * VRAM_BYTES;
@@ -100,7 +101,7 @@ void hr_frame(void* h, const uint8_t* buttons) {
         c.status = w[S_STATUS];
         uint8_t* slot = r->log.data();
         begin_frame(c, slot, buttons[e], kLogCap);
-        const Fast fst{c.ram, c.ramh, r->prg.data(), reinterpret_cast<const uint32_t*>(r->prg.data() + 0x8000)};
+        const Fast fst{c.ram, c.ramh, c.ram_end, r->prg.data(), reinterpret_cast<const uint32_t*>(r->prg.data() + 0x8000)};
         Hot hot{};
         hot_in(hot, c, fst);
         rf_pack(hot);

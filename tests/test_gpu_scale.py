@@ -8,7 +8,10 @@ engine run is compared with the reference's C++ core (oracle/_ref) on slices of 
   no-op starts up to 30, max-pool, max_steps 2000, frame stack 4; slices [0, 128), [16384, 16512) and
   [32640, 32768), i.e. the first, a middle and the last step slice of the engine (its 1,024 env groups run as
   four slices; the ragged tails of the device-to-host copies are covered by the API tests);
-* config 2 (the divergence-stress image) at 4,096 envs, slices [0, 128) and [3968, 4096).
+* config 2 (the divergence-stress image) at 4,096 envs, slices [0, 128) and [3968, 4096);
+* config 3's size, 262,144 envs (8,192 env groups: the step kernel runs them with its wide shared-memory
+  layout, 23 KB of RAM per CTA, where the two sizes above use the deep one), slices [0, 128),
+  [131072, 131200) and [262016, 262144), 300 steps.
 
 Every step compares, for every env of the slices: the stacked observation, reward, terminated, truncated and
 the ten info fields; for envs whose episode ended also final_obs, episode return and length; every 50 steps
@@ -158,4 +161,12 @@ def test_config2_divergent_4096_envs_lockstep_slices(oracle, rom_div):
     kw = dict(sticky=0.25, noop_max=30, maxpool=True, max_steps=2000, skip=4, frame_stack=4)
     stats = _run(oracle, rom_div, 4096, [(0, 128), (3968, 4096)], kw, scaled(2500), action_seed=4096)
     print("config2 4096 envs:", stats)
+    assert stats["episodes"] > 0
+
+
+def test_config3_262144_envs_wide_layout_lockstep_slices(oracle, rom):
+    kw = dict(sticky=0.25, noop_max=30, maxpool=True, max_steps=2000, skip=4, frame_stack=4)
+    stats = _run(oracle, rom, 262144, [(0, 128), (131072, 131200), (262016, 262144)], kw, scaled(300),
+                 action_seed=262144)
+    print("config3 262144 envs:", stats)
     assert stats["episodes"] > 0

@@ -459,11 +459,15 @@ def main():
         fenv.check()
         dt_max = shard.max_over_ranks(dt, device=dev)
         h2d = E * 8
-        d2h = E * (4 * 84 * 84 + 4 + 1 + 1 + 4 * 10 + 8 + 4) + (n_final * 4 * 84 * 84) // args.steps
+        # FastVecEnv reuses one pinned obs buffer and passes FME_HOST_OBS_IN_PLACE: frames 1..3 of every stack
+        # move down inside it on the host, so each step copies one new 84x84 frame per env, the scalars, and
+        # the full stacks of the ended envs' final_obs rows
+        d2h = E * (84 * 84 + 4 + 1 + 1 + 4 * 10 + 8 + 4) + (n_final * 4 * 84 * 84) // args.steps
         e2e = {"value": shard.job_throughput(world, E, args.steps, dt_max * 1000.0), "unit": UNIT,
                "h2d_bytes_per_step": h2d * world, "d2h_bytes_per_step": d2h * world,
-               "api": "FastVecEnv.step_arrays: fme_step with pinned host actions in and every output "
-                      "(stacked obs, rew, term, trunc, info, episode stats, final_obs rows) copied to host"}
+               "api": "FastVecEnv.step_arrays: fme_step_to_host with pinned host actions in and every output "
+                      "(stacked obs, rew, term, trunc, info, episode stats, final_obs rows) in pinned host "
+                      "memory; the stacks shift in place on the host, so only each env's new frame crosses"}
         fenv.close()
 
     peak, peak_kind = read_peaks()

@@ -414,6 +414,7 @@ __global__ void __launch_bounds__(32) k_render(RenderParams P) {
     RLayout L;
     L.fb = sm + RB_FB; L.vram = sm + RB_VRAM; L.pal = sm + RB_PAL; L.oam = sm + RB_OAM; L.stage = sm + RB_STAGE;
     L.lut = sm + RB_LUT; L.spr = reinterpret_cast<uint32_t*>(sm + RB_SPR); L.gv = sm + RB_GV;
+    L.bmask = reinterpret_cast<uint32_t*>(sm + RB_OBS);   // the resize output is written after the replays
     L.row_lo = band * BAND_ROWS; L.row_hi = L.row_lo + BAND_ROWS;
     if (lane < 16) reinterpret_cast<uint4*>(sm + RB_LUT)[lane] = reinterpret_cast<const uint4*>(d.lut)[lane];
     __syncwarp();

@@ -139,12 +139,14 @@ static_assert(RS_END <= SLAB_BYTES, "render scratch must fit the slab region");
 struct RLayout {
     uint8_t* fb; uint8_t* vram; uint8_t* pal; uint8_t* oam; uint8_t* stage; const uint8_t* lut;
     uint32_t* spr; uint8_t* gv;
+    uint32_t* bmask;   // 32 words: sprites of the line's list that cover each 8-dot block (scratch of the replay)
     int row_lo, row_hi;
 };
 __device__ __forceinline__ RLayout full_layout(uint8_t* sm) {
     RLayout L;
     L.fb = sm + RS_FB; L.vram = sm + RS_VRAM; L.pal = sm + RS_PAL; L.oam = sm + RS_OAM; L.stage = sm + RS_STAGE;
     L.lut = sm + RS_LUT; L.spr = reinterpret_cast<uint32_t*>(sm + RS_SPR); L.gv = sm + RS_GV;
+    L.bmask = reinterpret_cast<uint32_t*>(sm + RS_OBS);   // the resize output is written after the replays
     L.row_lo = 0; L.row_hi = SCREEN_H;
     return L;
 }
@@ -242,10 +244,17 @@ __device__ void render_slot(const uint8_t* slot, const RLayout& L, const Dev& d,
                 if (spr_on) {
                     uint32_t k0 = (uint32_t)g.y | (nsl << 8) | ((g.flags & (RF_LONG | RF_SPR_PAGE)) << 12) | (ver << 20);
                     if (k0 != skey0 || lo != skey1 || hi != skey2) {
+                        L.bmask[lane] = 0u;
+                        __syncwarp();
                         if ((uint32_t)lane < nsl) {
                             int i = (int)(((lane < 4 ? lo >> (8 * lane) : hi >> (8 * (lane - 4)))) & 0xffu);
                             srow_s[lane] = sprite_row(rs, g.flags, i, g.y);
-                            sinfo_s[lane] = sprite_info(rs, i);
+                            const uint32_t inf = sprite_info(rs, i);
+                            sinfo_s[lane] = inf;
+                            // the 8-dot blocks holding the sprite's dots x .. x+7 (dots past 255 do not exist)
+                            const uint32_t x = inf & 0xffu, b0 = x >> 3, b1 = (x + 7u) >> 3;
+                            atomicOr(&L.bmask[b0], 1u << lane);
+                            if (b1 != b0 && b1 < 32u) atomicOr(&L.bmask[b1], 1u << lane);
                         }
                         skey0 = k0; skey1 = lo; skey2 = hi;
                         __syncwarp();
@@ -254,7 +263,10 @@ __device__ void render_slot(const uint8_t* slot, const RLayout& L, const Dev& d,
                 const bool to_stage = max_mode && g.y == first_row;
                 const int xa = g.x0 + lane * 8;
                 uint32_t outw[2];
-                render8(rs, g, xa, spr_on ? nsl : 0u, srow_s, sinfo_s, gv, outw);
+                // candidates: the sprites covering either 8-dot block the lane's dots xa .. xa+7 touch (lanes
+                // past the segment's end draw nothing that is stored; their block index only stays in range)
+                const uint32_t cand = spr_on ? (L.bmask[(xa >> 3) & 31] | L.bmask[((xa + 7) >> 3) & 31]) : 0u;
+                render8(rs, g, xa, cand, srow_s, sinfo_s, gv, outw);
                 uint8_t* row = to_stage ? stage : fb + g.y * SCREEN_W;
                 if (xa < g.x1) {
                     if (xa + 8 <= g.x1 && (xa & 7) == 0) {
@@ -328,21 +340,32 @@ __device__ void resize_band(const uint8_t* fb, int row_lo, int dy_lo, int dy_hi,
 #pragma unroll
         for (int k = 0; k < AREA_XTAPS; k++) xw[q][k] = dx < OBS ? c_area.xw[k][dx] : 0.f;
     }
+    // A source row's horizontal sums do not depend on the output row that reads them, so the row shared by
+    // two consecutive output rows (240 / 84 is not whole) is summed once: the sums of the last row read are
+    // kept and reused when the next output row's first tap is that row.
+    int crow = -1;
+    float cb[3] = {0.f, 0.f, 0.f};
     for (int dy = dy_lo; dy < dy_hi; dy++) {
         float sacc[3] = {0.f, 0.f, 0.f};
         for (int m = 0; m < 6; m++) {
             float wy = c_area.yw[m][dy];
             if (wy == 0.f) break;
-            const uint8_t* row = fb + c_area.ys[m][dy] * SCREEN_W;
+            const int sr = c_area.ys[m][dy];
+            if (sr != crow) {
+                const uint8_t* row = fb + sr * SCREEN_W;
 #pragma unroll
-            for (int q = 0; q < 3; q++) {
-                float b = 0.f;
+                for (int q = 0; q < 3; q++) {
+                    float b = 0.f;
 #pragma unroll
-                for (int k = 0; k < AREA_XTAPS; k++) {
-                    if (xw[q][k] != 0.f) b = fadd(b, fmul((float)row[xs0[q] + k], xw[q][k]));
+                    for (int k = 0; k < AREA_XTAPS; k++) {
+                        if (xw[q][k] != 0.f) b = fadd(b, fmul((float)row[xs0[q] + k], xw[q][k]));
+                    }
+                    cb[q] = b;
                 }
-                sacc[q] = fadd(sacc[q], fmul(wy, b));
+                crow = sr;
             }
+#pragma unroll
+            for (int q = 0; q < 3; q++) sacc[q] = fadd(sacc[q], fmul(wy, cb[q]));
         }
 #pragma unroll
         for (int q = 0; q < 3; q++) {

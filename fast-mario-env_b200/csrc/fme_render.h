@@ -297,11 +297,12 @@ FME_HD void bg_tile(const RState& rs, uint32_t v, uint32_t bg_page, uint32_t& lo
 FME_HD uint32_t expand4(uint32_t n) { return (n * 0x00204081u) & 0x01010101u; }
 
 // The 8 output values of dots xa..xa+7 of segment g (bytes j of out[0..1]; dots outside the segment are
-// computed but must not be stored). srow/sinfo: the line's sprite rows (list order), nsl of them. gv: the
+// computed but must not be stored). srow/sinfo: the line's sprite rows (list order); cand: bit k set for each
+// list entry k that may cover one of the dots (every sprite that does is included). gv: the
 // output value of each of the 32 palette addresses (palette entry, through the gray LUT unless raw).
 // Per-dot decisions of nes_core.hpp:422-513 are made on 8-bit planes (bit 7-j = dot xa+j): background
 // pattern bits and palette select, left-edge hiding, first opaque sprite of the list, and its priority.
-FME_HD void render8(const RState& rs, const Seg& g, int xa, uint32_t nsl, const uint32_t* srow, const uint32_t* sinfo,
+FME_HD void render8(const RState& rs, const Seg& g, int xa, uint32_t cand, const uint32_t* srow, const uint32_t* sinfo,
                     const uint8_t* gv, uint32_t* out) {
     const uint32_t keep = xa >= 8 ? 0xffu : (1u << xa) - 1u;   // dots at x >= 8 (for left-edge hiding)
     uint32_t wlo = 0, whi = 0, am0 = 0, am1 = 0;
@@ -324,8 +325,13 @@ FME_HD void render8(const RState& rs, const Seg& g, int xa, uint32_t nsl, const 
     const uint32_t bo = wlo | whi;                               // opaque background dots
     am0 &= bo; am1 &= bo;
     uint32_t filled = 0, front_m = 0, p0 = 0, p1 = 0, q0 = 0, q1 = 0;
-    if ((g.flags & RF_SHOW_SPR) && nsl) {
-        for (uint32_t k = 0; k < nsl; k++) {
+    if ((g.flags & RF_SHOW_SPR) && cand) {
+        for (uint32_t m = cand; m; m &= m - 1u) {   // list order: the lowest entry first
+#if defined(__CUDA_ARCH__)
+            const uint32_t k = (uint32_t)__ffs((int)m) - 1u;
+#else
+            const uint32_t k = (uint32_t)__builtin_ctz(m);
+#endif
             const uint32_t inf = sinfo[k];
             const int o = xa - (int)(inf & 0xffu);
             if (o <= -8 || o >= 8) continue;

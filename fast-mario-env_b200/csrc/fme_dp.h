@@ -27,7 +27,7 @@ namespace fme {
 //         | cycles<<16 (3) | len<<19 (2) | PEN<<21 | IX<<22 (index X) | IY<<23 (index Y) | ZW<<24 (address wraps
 //         in page 0) | IND<<25 (pointer in page 0) | INX<<26 (pointer at W+X) | CMPA<<27 (computed address: I/O
 //         test, page penalty, ROM read) | PULL<<28 | PUSH<<29 | IMM<<30 | OK<<31
-// word 1: SEL (8: byte-permute nibbles of the ALU operands L and R in {A, X, Y, SP, M, 1, $FF, -}; for a
+// word 1: SEL (8: byte-permute nibbles of the ALU operands L and R in {A, X, Y, SP, M, 1, $FF, P}; for a
 //         branch or a flag operation: flag bit index (3) | value<<3) | FMASK<<8 (8: the flags the ALU result
 //         sets, in nes-py's layout) | CLS<<16 (2: logic, add, shift left, shift right) | LOP<<18 (2: pass R, or,
 //         and, eor) | BITF<<20 | INV<<21 | CIN<<22 (2: 0, 1, C) | DST<<24 (3) | PCM<<27 (2) | PF<<29 | JSR<<30
@@ -37,9 +37,9 @@ constexpr uint32_t D_PEN = 1u << 21, D_IX = 1u << 22, D_IY = 1u << 23, D_ZW = 1u
                    D_OK = 1u << 31;
 enum DCls : uint32_t { CL_LOGIC = 0, CL_ADD, CL_SHL, CL_SHR };
 enum DLop : uint32_t { LO_PASS = 0, LO_OR, LO_AND, LO_EOR };
-enum DByte : uint32_t { B_A = 0, B_X, B_Y, B_SP, B_M, B_ONE, B_FF };
+enum DByte : uint32_t { B_A = 0, B_X, B_Y, B_SP, B_M, B_ONE, B_FF, B_P };
 enum DCin : uint32_t { CI_0 = 0, CI_1, CI_C };
-enum DDst : uint32_t { DS_NONE = 0, DS_A, DS_X, DS_Y, DS_SP, DS_MEM };
+enum DDst : uint32_t { DS_NONE = 0, DS_A, DS_X, DS_Y, DS_SP, DS_MEM, DS_P };
 enum DPcm : uint32_t { PC_NEXT = 0, PC_JUMP, PC_BRANCH, PC_RTS };
 constexpr uint32_t D_BITF = 1u << 20, D_INV = 1u << 21, D_PF = 1u << 29, D_JSR = 1u << 30, D_BX = 1u << 31;
 enum DAm : uint32_t { AM_NONE = 0, AM_IMM, AM_DIR, AM_ZPX, AM_ZPY, AM_ABX, AM_ABY, AM_INX, AM_INY, AM_PULL, AM_PUSH };
@@ -164,6 +164,8 @@ inline uint2 make_dop(uint32_t ux, uint32_t uy) {
         case I_JSR: stk(AM_NONE, B_A, DS_NONE, 0, PC_JUMP, true); break;
         case I_SEC: flag(7, 1); break;
         case I_PHA: stk(AM_PUSH, B_A, DS_MEM, 0, PC_NEXT, false); break;
+        case I_PHP: stk(AM_PUSH, B_P, DS_MEM, 0, PC_NEXT, false); break;   // the status byte as stored
+        case I_PLP: stk(AM_PULL, B_M, DS_P, 0, PC_NEXT, false); break;     // the pulled byte, unchanged
         case I_JMP: stk(AM_NONE, B_A, DS_NONE, 0, PC_JUMP, false); break;
         case I_CLI: flag(5, 0); break;
         case I_RTS: stk(AM_PULL, B_M, DS_NONE, 0, PC_RTS, false); break;
@@ -183,7 +185,7 @@ inline uint2 make_dop(uint32_t ux, uint32_t uy) {
         case I_INX: reg(CL_ADD, B_X, B_ONE, DS_X, NZ); break;
         case I_NOP: stk(AM_NONE, B_A, DS_NONE, 0, PC_NEXT, false); break;
         case I_SED: flag(4, 1); break;
-        default: break;  // BRK, PHP, PLP, RTI, JMP (ind): exact path
+        default: break;  // BRK, RTI, JMP (ind): exact path
     }
     return d;
 }
@@ -264,8 +266,8 @@ FME_HD bool dp_exec(Hot& h, const Fast& f, const uint32_t* dops, bool run = true
     // operand: immediate, pulled byte, or memory (a ROM byte only at a computed address: static ROM operands
     // are immediates by now)
     const uint32_t m = (dx & D_IMM) ? W : pull ? p0 : (cmpa && ea >= 0x8000u) ? mrom : mram;
-    // ALU: L and R are bytes of {A, X, Y, SP, M, 1, $FF}
-    const uint32_t ops = byte_sel2(rf, m | 0x00ff0100u, dy);
+    // ALU: L and R are bytes of {A, X, Y, SP, M, 1, $FF, P}
+    const uint32_t ops = byte_sel2(rf, m | 0x00ff0100u | (P << 24), dy);
     const uint32_t L = ops & 0xffu, R = (ops >> 8) & 0xffu;
     const uint32_t Ri = R ^ ((dy & D_INV) ? 0xffu : 0u);
     const uint32_t cm = (dy >> 22) & 3u;
@@ -300,7 +302,7 @@ FME_HD bool dp_exec(Hot& h, const Fast& f, const uint32_t* dops, bool run = true
     const uint32_t nrf = (dst >= DS_A && dst <= DS_SP) ? ((rf & ~(0xffu << sh)) | (r << sh)) : rf;
     const uint32_t spd = (dx & D_PUSH) ? 0xffu : jsr ? 0xfeu : pull ? (pcm == PC_RTS ? 2u : 1u) : 0u;
     h.rf = ok ? nrf + (spd << 24) : rf;
-    h.p = ok ? p : P;
+    h.p = ok ? (dst == DS_P ? r : p) : P;   // PLP loads the status byte whole
     h.pc = ok ? pc : h.pc;
     h.ux = ok ? nd.x : dx;
     h.uy = ok ? nd.y : dy;

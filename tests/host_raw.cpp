@@ -130,4 +130,63 @@ int64_t hr_bad_ops(void* h, int e) { return static_cast<HostRaw*>(h)->words[(siz
 int64_t hr_status(void* h, int e) { return static_cast<HostRaw*>(h)->words[(size_t)e * S_WORDS + S_STATUS]; }
 void hr_destroy(void* h) { delete static_cast<HostRaw*>(h); }
 
+// One instruction at a time, from random states: the datapath (dp_exec, the step kernel's bulk path) against
+// the exact interpreter (Core::execute_op, which the lockstep tests pin to the reference). PRG is random
+// bytes, so every PRG address starts an instruction with random operand bytes; registers, status byte and
+// RAM are random. RAM is held whole in one buffer (ram_end 0x800) or split at `ram_end` across two buffers
+// (the step kernel's shared-memory / HBM layout). Only instructions the datapath commits are compared: pc,
+// A, X, Y, SP, P, the cycle count and all of RAM. Returns the number compared; *first_bad receives
+// (opcode << 16 | pc & 0xffff) of the first mismatch, or -1; hist[opc] counts the comparisons per opcode.
+int64_t hr_dp_check(uint64_t seed, int64_t trials, uint32_t ram_end, int32_t* first_bad, int64_t* hist) {
+    uint64_t s = seed * 0x9E3779B97F4A7C15ull + 1u;
+    auto rnd = [&]() -> uint32_t {  // xorshift64*
+        s ^= s >> 12; s ^= s << 25; s ^= s >> 27;
+        return (uint32_t)((s * 0x2545F4914F6CDD1Dull) >> 32);
+    };
+    std::vector<uint8_t> prg(0x8000 + (size_t)UOP_WORDS * 4, 0), chr(0x2000, 0), vram(VRAM_BYTES, 0);
+    std::vector<uint32_t> dops((size_t)UOP_WORDS, 0);
+    // exact side: one slab; datapath side: the RAM below ram_end in `lo`, the rest in `hi` (same layout)
+    std::vector<uint8_t> slab(SLAB_BYTES, 0), lo(SLAB_BYTES, 0), hi(SLAB_BYTES, 0);
+    tables::build_dtab(g_host_dtab);
+    *first_bad = -1;
+    int64_t compared = 0;
+    for (int64_t t = 0; t < trials; t++) {
+        if (t % 4096 == 0) {  // a new random PRG image every 4096 instructions
+            for (uint32_t i = 0; i < 0x8000u; i++) prg[i] = (uint8_t)rnd();
+            tables::build_uops(prg.data(), g_host_dtab, reinterpret_cast<uint32_t*>(prg.data() + 0x8000));
+            tables::build_dops(reinterpret_cast<const uint32_t*>(prg.data() + 0x8000), dops.data());
+        }
+        const uint32_t pc = 0x8000u | (rnd() & 0x7fffu);
+        const uint32_t a = rnd() & 0xffu, x = rnd() & 0xffu, y = rnd() & 0xffu, sp = rnd() & 0xffu, p = rnd() & 0xffu;
+        for (uint32_t m = 0; m < (uint32_t)RAM_BYTES; m++) {
+            const uint8_t v = (uint8_t)rnd();
+            slab[il(m)] = v;
+            (m < ram_end ? lo : hi)[il(m)] = v;
+        }
+        Hot h{};
+        h.pc = pc; h.a = a; h.x = x; h.y = y; h.sp = sp; h.p = p; h.exec_at = 0; h.thresh = 1 << 30;
+        rf_pack(h);
+        dfetch(h, dops.data());
+        if (!(h.ux & D_OK)) continue;
+        const Fast f{lo.data(), hi.data(), ram_end, prg.data(), reinterpret_cast<const uint32_t*>(prg.data() + 0x8000)};
+        if (!dp_exec(h, f, dops.data(), true)) continue;   // a computed I/O address: the exact path's case
+        rf_unpack(h);
+        Core c{};
+        c.ram = c.ramh = slab.data(); c.ram_end = RAM_BYTES;
+        c.oam = slab.data() + SLAB_OAM_OFF; c.pal = slab.data() + SLAB_PAL_OFF; c.vram = vram.data();
+        c.cart.prg = prg.data(); c.cart.chr = chr.data();
+        c.pc = pc; c.a = a; c.x = x; c.y = y; c.sp = sp; c.p = p;
+        const uint32_t opc = prg[pc & 0x7fffu];
+        const int32_t S = c.execute_op(opc);
+        bool same = h.pc == c.pc && h.a == c.a && h.x == c.x && h.y == c.y && h.sp == c.sp && h.p == c.p &&
+                    h.exec_at == (S >= 1 ? S : 1);
+        for (uint32_t m = 0; same && m < (uint32_t)RAM_BYTES; m++)
+            same = (m < ram_end ? lo : hi)[il(m)] == slab[il(m)];
+        compared++;
+        hist[opc]++;
+        if (!same && *first_bad < 0) *first_bad = (int32_t)((opc << 16) | (pc & 0xffffu));
+    }
+    return compared;
+}
+
 }  // extern "C"

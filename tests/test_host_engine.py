@@ -48,6 +48,8 @@ def host(tmp_path_factory):
         f.restype = ctypes.c_int64
         f.argtypes = [P, ctypes.c_int]
     H.hr_destroy.argtypes = [P]
+    H.hr_dp_check.restype = ctypes.c_int64
+    H.hr_dp_check.argtypes = [ctypes.c_uint64, ctypes.c_int64, ctypes.c_uint32, P, P]
     return H
 
 
@@ -76,3 +78,24 @@ def test_host_build_of_the_engine_matches_reference(host, oracle, image):
             assert host.hr_status(h, i) == 0
     finally:
         host.hr_destroy(h)
+
+
+# the datapath runs every official opcode whose memory accesses are RAM or PRG only, i.e. all of them except
+# BRK ($00), RTI ($40) and JMP (ind) ($6C), which stay on the exact path
+_EXACT_ONLY = {0x00, 0x40, 0x6C}
+
+
+@pytest.mark.parametrize("ram_end", [0x800, 0x600, 0x2E0], ids=["whole_ram", "split_0600", "split_02e0"])
+def test_datapath_matches_exact_interpreter_per_instruction(host, ram_end):
+    """dp_exec against Core::execute_op on random PRG bytes, registers, status bytes and RAM: pc, registers,
+    status, cycles and RAM after each committed instruction, with RAM whole or split across two buffers."""
+    bad = ctypes.c_int32(0)
+    hist = np.zeros(256, np.int64)
+    n = host.hr_dp_check(11 + ram_end, 400_000, ram_end, ctypes.byref(bad), hist.ctypes.data)
+    assert bad.value == -1, f"opcode ${bad.value >> 16:02X} at ${bad.value & 0xffff:04X} differs"
+    assert n > 100_000
+    from fast_mario_env_b200 import asm6502
+    official = set(asm6502.OPCODES.values())
+    covered = {opc for opc in range(256) if hist[opc] > 0}
+    assert official - _EXACT_ONLY <= covered, sorted(official - _EXACT_ONLY - covered)
+    assert not covered & _EXACT_ONLY

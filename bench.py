@@ -476,7 +476,11 @@ def main():
     traffic_per_step = committed_traffic(top)
     roofline = {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
                 "traffic": traffic_per_step * E if traffic_per_step else None,
-                "kernel": top, "kernel_ms": kernel_ms, "algorithmic_bytes_per_env_step": ALGO_BYTES[top],
+                "kernel": top, "kernel_ms": kernel_ms,
+                "kernel_ms_note": "spans per step, not single-launch durations: k_step = the step's start until "
+                                  "the last of its 4 concurrent emulation slices ends (earlier slices' renders "
+                                  "overlap it); k_render = the rest of the step (the last slice's render)",
+                "algorithmic_bytes_per_env_step": ALGO_BYTES[top],
                 "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured" else "fallback 6.65 TB/s",
                 "note": "the env step is an issue-bound integer interpreter: the HBM fraction is reported as the "
                         "contract asks, the binding roof is roofline.issue"}
